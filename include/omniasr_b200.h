@@ -1,0 +1,124 @@
+/* omniASR-LLM decoder attention hot path on B200 (sm_100a): the C ABI.
+ *
+ * Every entry point takes plain device pointers, element strides, host ints and a CUDA stream,
+ * launches asynchronously on that stream, never synchronises, never allocates, and returns
+ * OMNIASR_OK or an error code (omniasr_last_error() has the message). Launch grids depend only on
+ * host ints, so every call can be captured in a CUDA graph; lengths, positions and pointers are
+ * read on the device.
+ *
+ * Tensors: `dtype` is OMNIASR_BF16 or OMNIASR_F32 for q / k / v / out; head_dim (`dim`) is one of
+ * 16, 32, 64, 128, 256, 512; the innermost (head_dim) stride of every tensor is 1, the other
+ * strides are in elements and every pointer / stride must keep 16-byte alignment. Caches are
+ * [rows, heads, len, dim] with strides (stride_row, stride_head, stride_pos); k and v caches of
+ * one call share their strides. Index tensors (lengths, positions, slots) are int64.
+ *
+ * `status` (may be NULL) is a device int the kernels OR error bits into: 1 = an index read from a
+ * tensor (length, position, slot, beam pointer, parent) was outside its tensor and the access was
+ * skipped; 2 = a bounded device wait gave up. The kernels never trap.
+ *
+ * Each declaration names the function of the reference (Wataru-Nakata/omniasr-trt, Python) it
+ * replaces, as path:line within that project.
+ */
+#ifndef OMNIASR_B200_H
+#define OMNIASR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OMNIASR_BF16 0
+#define OMNIASR_F32 1
+
+#define OMNIASR_OK 0
+#define OMNIASR_ERR_ARGUMENT 1    /* a shape, stride, pointer alignment or size is invalid */
+#define OMNIASR_ERR_UNSUPPORTED 2 /* dtype or head_dim not supported */
+#define OMNIASR_ERR_WORKSPACE 3   /* workspace smaller than omniasr_attention_workspace() */
+#define OMNIASR_ERR_CUDA 4        /* a CUDA launch failed */
+#define OMNIASR_ERR_DEVICE 5      /* the current device cannot run sm_100a code */
+
+/* Workspace kinds for omniasr_attention_workspace(). */
+#define OMNIASR_DECODE 0
+#define OMNIASR_DRAFT 1
+#define OMNIASR_BEAM 2
+
+/* Version of this ABI (bumped on any signature change). */
+int omniasr_abi_version(void);
+
+/* Message of the last error returned on this host thread ("" if none). */
+const char* omniasr_last_error(void);
+
+/* 1 if `device` can run this library's kernels (compute capability 10.0), else 0.
+ * Replaces omniasr_trt/kernels.py:25-26 (`available`). */
+int omniasr_device_supported(int device);
+
+/* The reference's split rule: key splits (a power of two, about `programs` programs in all) and
+ * the keys each split covers. Host only. Replaces omniasr_trt/kernels.py:393-400 (`splits_for`). */
+int omniasr_splits_for(int rows, int heads, int keys, int block, int programs, int* splits, int* chunk);
+
+/* Bytes of workspace an attention call of this shape needs on the current device (the split
+ * partials; the reference allocates them inside its wrappers, omniasr_trt/kernels.py:319-320,
+ * :349-350, :416-417). kind: OMNIASR_DECODE (per_group = 1), OMNIASR_DRAFT (per_group = tokens),
+ * OMNIASR_BEAM (per_group = beams, gen_keys = generated-cache length). */
+size_t omniasr_attention_workspace(int kind, int dtype, int groups, int per_group, int heads, int dim,
+                                   int64_t keys, int64_t gen_keys);
+
+/* RoPE of q and k at pos[n] (interleaved pairs, fp32, table cs [cs_positions, dim/2, 2] fp32) and
+ * the KV-cache append: rotated k and raw v of token n written at cache row slots[n] (NULL: n) and
+ * position cache_pos[n] (NULL: pos[n]); rotated q written to q_out [n, heads, dim] contiguous.
+ * qkv is [n, 3 * heads * dim] with row stride qkv_stride. Bit-exact with the reference.
+ * Replaces omniasr_trt/kernels.py:294-306 (`rope_kv`) and its kernel kernels.py:31-54. */
+int omniasr_rope_kv(const void* qkv, int64_t qkv_stride, const float* cs, int64_t cs_positions, const int64_t* pos,
+                    const int64_t* slots, const int64_t* cache_pos, void* q_out, void* k_cache, void* v_cache,
+                    int64_t cache_rows, int64_t cache_len, int64_t stride_row, int64_t stride_head,
+                    int64_t stride_pos, int n, int heads, int dim, int dtype, int* status, cudaStream_t stream);
+
+/* Flash-decode: q [batch, heads, dim] contiguous, row b attends to keys [0, lengths[b]) of cache
+ * row b (all within the first `keys`, which fixes the grid); out [batch, heads, dim] contiguous in
+ * q's dtype. A row of length 0 gets zeros.
+ * Replaces omniasr_trt/kernels.py:406-423 (`decode_attention`: _attn_split + _attn_combine). */
+int omniasr_decode_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                             int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                             const int64_t* lengths, void* out, int batch, int heads, int dim, int keys, float scale,
+                             int dtype, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
+
+/* Draft verification: q [batch * tokens, heads, dim], row b's queries at rows b*tokens ..
+ * b*tokens + tokens - 1; query i of row b attends to keys [0, lengths[b] + i) of cache row b (all
+ * within the first `keys`). out like q.
+ * Replaces omniasr_trt/kernels.py:338-358 (`draft_attention`: _beam_ctx CAUSAL + _beam_combine). */
+int omniasr_draft_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                            int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                            const int64_t* lengths, void* out, int batch, int tokens, int heads, int dim, int keys,
+                            float scale, int dtype, void* workspace, size_t workspace_bytes, int* status,
+                            cudaStream_t stream);
+
+/* Beam attention: q [groups * beams, heads, dim] (input g's beams at rows g*beams ..); row r
+ * attends to its input's context keys [0, ctx_len[g]) of kc/vc row g (all within `ctx_keys`) and
+ * to its generated keys j < gen_len[r], key j read from kg/vg row ptr[r * ptr_stride + j] (int32)
+ * at position j. out like q; a row with no keys gets zeros.
+ * Replaces omniasr_trt/kernels.py:309-332 (`beam_attention`: _beam_ctx + _beam_gen + _beam_combine). */
+int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_t ctx_rows, int64_t ctx_len_cap,
+                           int64_t ctx_stride_row, int64_t ctx_stride_head, int64_t ctx_stride_pos,
+                           const int64_t* ctx_len, const void* kg, const void* vg, int64_t gen_rows,
+                           int64_t gen_len_cap, int64_t gen_stride_row, int64_t gen_stride_head,
+                           int64_t gen_stride_pos, const int32_t* ptr, int64_t ptr_stride, const int64_t* gen_len,
+                           void* out, int groups, int beams, int heads, int dim, int ctx_keys, float scale, int dtype,
+                           void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
+
+/* Beam reorder: dst row r (r < rows) = src row parent[r], byte-exact; rows are row_bytes long,
+ * strides in bytes; parent is int32 (parent_is_int64 = 0) or int64. src and dst must not overlap.
+ * Replaces the K/V `index_select(0, parent)` of omniasr_trt/llm.py:237-238 and the pointer /
+ * history gathers `ptr[parent]`, `hist[parent]` of omniasr_trt/beam.py:175-176. */
+int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_rows, void* dst,
+                           int64_t dst_row_stride, const void* parent, int parent_is_int64, int rows,
+                           int64_t row_bytes, int* status, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OMNIASR_B200_H */

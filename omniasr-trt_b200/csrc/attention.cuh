@@ -1,0 +1,62 @@
+// Split-KV attention over a KV cache: plan, partial-result layout and internal launchers.
+//
+// A "group" is a set of `nq` query rows that share one cache row's keys:
+//   * decode (q_len 1):          group = batch row, nq = 1
+//   * draft verify (q_len 1+k):  group = batch row, nq = 1+k, causal (query i sees lengths[g] + i keys)
+//   * beam context:              group = input, nq = beams (every beam sees ctx_len[g] keys)
+//   * beam generated part:       group = beam row, nq = 1, key j read from cache row ptr[r, j]
+// Each CTA handles one (group, head, key split, query block); it writes an unnormalised partial
+// output and its (max, sum) statistics, and a combine kernel merges the splits.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+namespace omni {
+
+enum DType : int { kBF16 = 0, kF32 = 1 };
+
+struct SplitArgs {
+  const void* q;  // [rows_q, heads, D], contiguous; row of query i of group g = g * nq + i
+  const void* k;  // cache [cache_rows, heads, cache_len, D] with strides s_kb, s_kh, s_ks (elements)
+  const void* v;  // same strides as k
+  int64_t s_kb, s_kh, s_ks;
+  int64_t cache_rows, cache_len;
+  const int64_t* lengths;  // [groups]
+  const int32_t* ptr;      // gather mode only: [groups, ptr_stride] source cache row of key j
+  int64_t ptr_stride;
+  float* part_o;          // [rows_q, heads, st, D]
+  float* part_ml;         // [rows_q, heads, st, 2] (max in log2 units, sum)
+  int st;                 // splits held per (row, head) in the partial arrays
+  int sp_offset;          // first split index written by this launch
+  int heads, nq, causal, chunk, qblocks;
+  int64_t key_bound;      // splits * chunk: keys the launch covers
+  float qscale;           // softmax scale * log2(e)
+  int* status;
+};
+
+struct SplitPlan {
+  int nqb;      // queries per CTA (compile-time variant: 1, 2, 4 or 8)
+  int qblocks;  // CTAs per group along the queries
+  int splits;   // key splits
+  int chunk;    // keys per split (a multiple of the tile)
+};
+
+// Key-split plan for `units` (group, head) pairs over `keys` keys.
+SplitPlan plan_split(int dtype, int dim, int groups, int heads, int nq, int64_t keys);
+
+// Bytes of the partial arrays for rows_q query rows with st splits each.
+size_t partial_bytes(int64_t rows_q, int heads, int st, int dim);
+void carve_partials(void* ws, int64_t rows_q, int heads, int st, int dim, float** part_o, float** part_ml);
+
+cudaError_t launch_split(int dtype, int dim, bool gather, const SplitPlan& plan, const SplitArgs& a, int groups,
+                         cudaStream_t stream);
+cudaError_t launch_combine(int dtype, int dim, const float* part_o, const float* part_ml, void* out,
+                           int64_t rows_heads, int st, cudaStream_t stream);
+
+bool dim_supported(int dtype, int dim);
+int device_sm_count();
+
+}  // namespace omni

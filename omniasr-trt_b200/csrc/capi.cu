@@ -1,0 +1,342 @@
+// extern "C" entry points (include/omniasr_b200.h): argument checks, split plans, launches.
+
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "attention.cuh"
+#include "gather.cuh"
+#include "omniasr_b200.h"
+#include "rope_kv.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int ok() {
+  g_error.clear();
+  return OMNIASR_OK;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(OMNIASR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int esize(int dtype) { return dtype == OMNIASR_BF16 ? 2 : 4; }
+
+bool stride_ok(int64_t stride, int dtype) { return stride >= 0 && (stride * esize(dtype)) % 16 == 0; }
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(OMNIASR_ERR_DEVICE, "no CUDA device");
+  if (!omniasr_device_supported(dev))
+    return fail(OMNIASR_ERR_DEVICE, "device %d is not compute capability 10.0 (sm_100a code)", dev);
+  return OMNIASR_OK;
+}
+
+int check_common(int dtype, int dim, int heads) {
+  if (dtype != OMNIASR_BF16 && dtype != OMNIASR_F32) return fail(OMNIASR_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (!omni::dim_supported(dtype, dim))
+    return fail(OMNIASR_ERR_UNSUPPORTED, "head_dim %d (supported: 16, 32, 64, 128, 256, 512)", dim);
+  if (heads <= 0 || heads > 65535) return fail(OMNIASR_ERR_ARGUMENT, "heads %d", heads);
+  return check_device();
+}
+
+int check_cache(const char* name, const void* k, const void* v, int64_t rows, int64_t len, int64_t s_row,
+                int64_t s_head, int64_t s_pos, int heads, int dim, int dtype) {
+  if (!k || !v) return fail(OMNIASR_ERR_ARGUMENT, "%s: null cache pointer", name);
+  if (!aligned16(k) || !aligned16(v)) return fail(OMNIASR_ERR_ARGUMENT, "%s: cache not 16-byte aligned", name);
+  if (!stride_ok(s_row, dtype) || !stride_ok(s_head, dtype) || !stride_ok(s_pos, dtype))
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: cache strides (%lld, %lld, %lld) must keep 16-byte alignment", name,
+                (long long)s_row, (long long)s_head, (long long)s_pos);
+  if (rows < 0 || len < 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: cache extents", name);
+  if (s_pos < dim && len > 1) return fail(OMNIASR_ERR_ARGUMENT, "%s: positions overlap (stride %lld < dim %d)", name,
+                                          (long long)s_pos, dim);
+  (void)heads;
+  return OMNIASR_OK;
+}
+
+// One split pass + combine over `groups` groups of `nq` queries.
+struct AttnPass {
+  omni::SplitPlan plan;
+  int st;
+};
+
+}  // namespace
+
+extern "C" {
+
+int omniasr_abi_version(void) { return 1; }
+
+const char* omniasr_last_error(void) { return g_error.c_str(); }
+
+int omniasr_device_supported(int device) {
+  static int cache[64] = {0};  // 0 unknown, 1 yes, 2 no
+  if (device < 0) return 0;
+  if (device < 64 && cache[device]) return cache[device] == 1;
+  int major = 0, minor = 0;
+  int ok_ = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) == cudaSuccess &&
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) == cudaSuccess &&
+            major == 10 && minor == 0;
+  if (device < 64) cache[device] = ok_ ? 1 : 2;
+  return ok_;
+}
+
+int omniasr_splits_for(int rows, int heads, int keys, int block, int programs, int* splits, int* chunk) {
+  if (rows <= 0 || heads <= 0 || block <= 0 || !splits || !chunk)
+    return fail(OMNIASR_ERR_ARGUMENT, "splits_for: rows %d heads %d block %d", rows, heads, block);
+  int want = programs / (rows * heads);
+  if (want < 1) want = 1;
+  int s = 1;
+  while (s * 2 <= want && (int64_t)s * 2 * block <= keys) s *= 2;
+  const int c = (keys + s - 1) / s;
+  *splits = s;
+  *chunk = (c + block - 1) / block * block;
+  return ok();
+}
+
+size_t omniasr_attention_workspace(int kind, int dtype, int groups, int per_group, int heads, int dim, int64_t keys,
+                                   int64_t gen_keys) {
+  if (groups <= 0 || per_group <= 0 || heads <= 0 || !omni::dim_supported(dtype, dim)) return 0;
+  const int64_t rows_q = (int64_t)groups * per_group;
+  if (kind == OMNIASR_BEAM) {
+    const omni::SplitPlan c = omni::plan_split(dtype, dim, groups, heads, per_group, keys);
+    const omni::SplitPlan g = omni::plan_split(dtype, dim, (int)rows_q, heads, 1, gen_keys);
+    return omni::partial_bytes(rows_q, heads, c.splits + g.splits, dim);
+  }
+  const omni::SplitPlan p = omni::plan_split(dtype, dim, groups, heads, kind == OMNIASR_DRAFT ? per_group : 1, keys);
+  return omni::partial_bytes(rows_q, heads, p.splits, dim);
+}
+
+int omniasr_rope_kv(const void* qkv, int64_t qkv_stride, const float* cs, int64_t cs_positions, const int64_t* pos,
+                    const int64_t* slots, const int64_t* cache_pos, void* q_out, void* k_cache, void* v_cache,
+                    int64_t cache_rows, int64_t cache_len, int64_t stride_row, int64_t stride_head,
+                    int64_t stride_pos, int n, int heads, int dim, int dtype, int* status, cudaStream_t stream) {
+  if (int e = check_common(dtype, dim, heads)) return e;
+  if (n < 0) return fail(OMNIASR_ERR_ARGUMENT, "rope_kv: n %d", n);
+  if (n == 0) return ok();
+  if (!qkv || !cs || !pos || !q_out) return fail(OMNIASR_ERR_ARGUMENT, "rope_kv: null pointer");
+  if (!aligned16(qkv) || !aligned16(cs) || !aligned16(q_out) || !stride_ok(qkv_stride, dtype))
+    return fail(OMNIASR_ERR_ARGUMENT, "rope_kv: qkv / cs / q_out must be 16-byte aligned");
+  if (qkv_stride < 3LL * heads * dim) return fail(OMNIASR_ERR_ARGUMENT, "rope_kv: qkv row stride %lld < 3*H*D",
+                                                  (long long)qkv_stride);
+  if (int e = check_cache("rope_kv", k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head, stride_pos,
+                          heads, dim, dtype))
+    return e;
+  omni::RopeArgs a;
+  a.qkv = qkv;
+  a.qkv_stride = qkv_stride;
+  a.cs = cs;
+  a.cs_positions = cs_positions;
+  a.pos = pos;
+  a.slots = slots;
+  a.cache_pos = cache_pos;
+  a.q_out = q_out;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.s_kb = stride_row;
+  a.s_kh = stride_head;
+  a.s_ks = stride_pos;
+  a.cache_rows = cache_rows;
+  a.cache_len = cache_len;
+  a.heads = heads;
+  a.status = status;
+  return cuda_status(omni::launch_rope_kv(dtype, dim, a, n, stream), "rope_kv launch");
+}
+
+static int group_attention(const char* name, const void* q, const void* k_cache, const void* v_cache,
+                           int64_t cache_rows, int64_t cache_len, int64_t stride_row, int64_t stride_head,
+                           int64_t stride_pos, const int64_t* lengths, void* out, int groups, int nq, int causal,
+                           int heads, int dim, int keys, float scale, int dtype, void* workspace,
+                           size_t workspace_bytes, int* status, cudaStream_t stream) {
+  if (int e = check_common(dtype, dim, heads)) return e;
+  if (groups < 0 || nq <= 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: batch %d tokens %d", name, groups, nq);
+  if (groups == 0) return ok();
+  if (!q || !out || !lengths) return fail(OMNIASR_ERR_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(q) || !aligned16(out)) return fail(OMNIASR_ERR_ARGUMENT, "%s: q / out not 16-byte aligned", name);
+  if (int e = check_cache(name, k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head, stride_pos, heads,
+                          dim, dtype))
+    return e;
+  if (groups > cache_rows) return fail(OMNIASR_ERR_ARGUMENT, "%s: %d rows but the cache has %lld", name, groups,
+                                       (long long)cache_rows);
+  if (keys < 0 || keys > cache_len)
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: keys %d outside [0, cache length %lld]", name, keys, (long long)cache_len);
+  const omni::SplitPlan plan = omni::plan_split(dtype, dim, groups, heads, nq, keys);
+  const int64_t rows_q = (int64_t)groups * nq;
+  const size_t need = omni::partial_bytes(rows_q, heads, plan.splits, dim);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
+                workspace ? workspace_bytes : (size_t)0, need);
+  float *po, *pml;
+  omni::carve_partials(workspace, rows_q, heads, plan.splits, dim, &po, &pml);
+  omni::SplitArgs a{};
+  a.q = q;
+  a.k = k_cache;
+  a.v = v_cache;
+  a.s_kb = stride_row;
+  a.s_kh = stride_head;
+  a.s_ks = stride_pos;
+  a.cache_rows = cache_rows;
+  a.cache_len = cache_len;
+  a.lengths = lengths;
+  a.part_o = po;
+  a.part_ml = pml;
+  a.st = plan.splits;
+  a.sp_offset = 0;
+  a.heads = heads;
+  a.nq = nq;
+  a.causal = causal;
+  a.chunk = plan.chunk;
+  a.qblocks = plan.qblocks;
+  a.key_bound = (int64_t)plan.splits * plan.chunk;
+  a.qscale = scale * omni::kLog2e;
+  a.status = status;
+  if (int e = cuda_status(omni::launch_split(dtype, dim, false, plan, a, groups, stream), "split launch")) return e;
+  return cuda_status(omni::launch_combine(dtype, dim, po, pml, out, rows_q * heads, plan.splits, stream),
+                     "combine launch");
+}
+
+int omniasr_decode_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                             int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                             const int64_t* lengths, void* out, int batch, int heads, int dim, int keys, float scale,
+                             int dtype, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+  return group_attention("decode_attention", q, k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                         stride_pos, lengths, out, batch, 1, 0, heads, dim, keys, scale, dtype, workspace,
+                         workspace_bytes, status, stream);
+}
+
+int omniasr_draft_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                            int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                            const int64_t* lengths, void* out, int batch, int tokens, int heads, int dim, int keys,
+                            float scale, int dtype, void* workspace, size_t workspace_bytes, int* status,
+                            cudaStream_t stream) {
+  return group_attention("draft_attention", q, k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                         stride_pos, lengths, out, batch, tokens, 1, heads, dim, keys, scale, dtype, workspace,
+                         workspace_bytes, status, stream);
+}
+
+int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_t ctx_rows, int64_t ctx_len_cap,
+                           int64_t ctx_stride_row, int64_t ctx_stride_head, int64_t ctx_stride_pos,
+                           const int64_t* ctx_len, const void* kg, const void* vg, int64_t gen_rows,
+                           int64_t gen_len_cap, int64_t gen_stride_row, int64_t gen_stride_head,
+                           int64_t gen_stride_pos, const int32_t* ptr, int64_t ptr_stride, const int64_t* gen_len,
+                           void* out, int groups, int beams, int heads, int dim, int ctx_keys, float scale, int dtype,
+                           void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+  const char* name = "beam_attention";
+  if (int e = check_common(dtype, dim, heads)) return e;
+  if (groups < 0 || beams <= 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: groups %d beams %d", name, groups, beams);
+  if (groups == 0) return ok();
+  if (!q || !out || !ctx_len || !gen_len || !ptr) return fail(OMNIASR_ERR_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(q) || !aligned16(out)) return fail(OMNIASR_ERR_ARGUMENT, "%s: q / out not 16-byte aligned", name);
+  if (int e = check_cache("beam_attention (context)", kc, vc, ctx_rows, ctx_len_cap, ctx_stride_row, ctx_stride_head,
+                          ctx_stride_pos, heads, dim, dtype))
+    return e;
+  if (int e = check_cache("beam_attention (generated)", kg, vg, gen_rows, gen_len_cap, gen_stride_row,
+                          gen_stride_head, gen_stride_pos, heads, dim, dtype))
+    return e;
+  const int64_t rows = (int64_t)groups * beams;
+  if (groups > ctx_rows) return fail(OMNIASR_ERR_ARGUMENT, "%s: %d inputs, context cache has %lld rows", name, groups,
+                                     (long long)ctx_rows);
+  if (rows > gen_rows) return fail(OMNIASR_ERR_ARGUMENT, "%s: %lld rows, generated cache has %lld", name,
+                                   (long long)rows, (long long)gen_rows);
+  if (ctx_keys < 0 || ctx_keys > ctx_len_cap)
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: ctx_keys %d outside [0, %lld]", name, ctx_keys, (long long)ctx_len_cap);
+  if (ptr_stride < gen_len_cap) return fail(OMNIASR_ERR_ARGUMENT, "%s: ptr row stride %lld < generated length %lld",
+                                            name, (long long)ptr_stride, (long long)gen_len_cap);
+  const omni::SplitPlan pc = omni::plan_split(dtype, dim, groups, heads, beams, ctx_keys);
+  const omni::SplitPlan pg = omni::plan_split(dtype, dim, (int)rows, heads, 1, gen_len_cap);
+  const int st = pc.splits + pg.splits;
+  const size_t need = omni::partial_bytes(rows, heads, st, dim);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
+                workspace ? workspace_bytes : (size_t)0, need);
+  float *po, *pml;
+  omni::carve_partials(workspace, rows, heads, st, dim, &po, &pml);
+  omni::SplitArgs a{};
+  a.q = q;
+  a.k = kc;
+  a.v = vc;
+  a.s_kb = ctx_stride_row;
+  a.s_kh = ctx_stride_head;
+  a.s_ks = ctx_stride_pos;
+  a.cache_rows = ctx_rows;
+  a.cache_len = ctx_len_cap;
+  a.lengths = ctx_len;
+  a.part_o = po;
+  a.part_ml = pml;
+  a.st = st;
+  a.sp_offset = 0;
+  a.heads = heads;
+  a.nq = beams;
+  a.causal = 0;
+  a.chunk = pc.chunk;
+  a.qblocks = pc.qblocks;
+  a.key_bound = (int64_t)pc.splits * pc.chunk;
+  a.qscale = scale * omni::kLog2e;
+  a.status = status;
+  if (int e = cuda_status(omni::launch_split(dtype, dim, false, pc, a, groups, stream), "context split launch"))
+    return e;
+  omni::SplitArgs b = a;
+  b.k = kg;
+  b.v = vg;
+  b.s_kb = gen_stride_row;
+  b.s_kh = gen_stride_head;
+  b.s_ks = gen_stride_pos;
+  b.cache_rows = gen_rows;
+  b.cache_len = gen_len_cap;
+  b.lengths = gen_len;
+  b.ptr = ptr;
+  b.ptr_stride = ptr_stride;
+  b.sp_offset = pc.splits;
+  b.nq = 1;
+  b.chunk = pg.chunk;
+  b.qblocks = 1;
+  b.key_bound = (int64_t)pg.splits * pg.chunk;
+  if (int e = cuda_status(omni::launch_split(dtype, dim, true, pg, b, (int)rows, stream), "generated split launch"))
+    return e;
+  return cuda_status(omni::launch_combine(dtype, dim, po, pml, out, rows * heads, st, stream), "combine launch");
+}
+
+int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_rows, void* dst,
+                           int64_t dst_row_stride, const void* parent, int parent_is_int64, int rows,
+                           int64_t row_bytes, int* status, cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (rows < 0 || row_bytes < 0 || src_rows < 0) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: sizes");
+  if (rows == 0 || row_bytes == 0) return ok();
+  if (!src || !dst || !parent) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: null pointer");
+  if (src_row_stride < row_bytes && src_rows > 1) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: src rows overlap");
+  if (dst_row_stride < row_bytes && rows > 1) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: dst rows overlap");
+  const char* s0 = static_cast<const char*>(src);
+  const char* s1 = s0 + (src_rows > 0 ? (src_rows - 1) * src_row_stride + row_bytes : 0);
+  const char* d0 = static_cast<const char*>(dst);
+  const char* d1 = d0 + (int64_t)(rows - 1) * dst_row_stride + row_bytes;
+  if (d0 < s1 && s0 < d1) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: src and dst overlap");
+  omni::GatherArgs a;
+  a.src = src;
+  a.src_stride = src_row_stride;
+  a.dst = dst;
+  a.dst_stride = dst_row_stride;
+  a.parent = parent;
+  a.parent64 = parent_is_int64 ? 1 : 0;
+  a.src_rows = src_rows;
+  a.row_bytes = row_bytes;
+  a.status = status;
+  return cuda_status(omni::launch_gather(a, rows, stream), "reorder_gather launch");
+}
+
+}  // extern "C"

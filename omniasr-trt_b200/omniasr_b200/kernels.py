@@ -1,0 +1,242 @@
+"""B200 (sm_100a) kernels behind the Python API of ``omniasr_trt.kernels`` (Wataru-Nakata/omniasr-trt).
+
+Same names, arguments, results and edge semantics as the reference module
+(``omniasr_trt/kernels.py:25-423``), so its decoders (``decode.py``, ``spec.py``, ``beam.py``) and their
+CUDA-graph capture run on these kernels unchanged:
+
+* :func:`rope_kv` -- RoPE of q and k at each token's position and the KV-cache append, bit-exact with
+  ``modeling.apply_rope`` (``kernels.py:294-306``);
+* :func:`decode_attention` -- one query per row, split-KV flash-decode (``kernels.py:406-423``);
+* :func:`draft_attention` -- a row's 1 + k draft queries, causal within them (``kernels.py:338-358``);
+* :func:`beam_attention` -- beams over their input's shared context plus their own generated keys through
+  the pointer history (``kernels.py:309-332``);
+* :func:`reorder_gather` -- the beam reorder ``dst[r] = src[parent[r]]``, byte-exact (``llm.py:237-238``,
+  ``beam.py:175-176``).
+
+Each call is a launch (or two) of hand-written CUDA through the C ABI of ``include/omniasr_b200.h`` on the
+current stream; outputs and split workspaces are allocated with ``torch.empty`` on the caller's device (from the
+graph pool during a capture). There is no other code path: on a CUDA device without the built library every
+function raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+ATTN = {"block": 64, "warps": 8, "stages": 2, "programs": 264}  # accepted and ignored (reference launch knobs)
+DRAFT_ATTN = {"block": 32, "warps": 4, "stages": 2, "programs": 264}
+
+_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+_status: dict[int, torch.Tensor] = {}
+
+
+def available(device: torch.device) -> bool:
+    """True on a CUDA device these kernels run on (compute capability 10.0).
+
+    Raises on a CUDA device when the library is missing: the product path has no silent fallback.
+    """
+    device = torch.device(device)
+    if device.type != "cuda" or not torch.cuda.is_available():
+        return False
+    lib = _lib.load()
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return bool(lib.omniasr_device_supported(index))
+
+
+def status_word(device: torch.device | int | None = None) -> torch.Tensor:
+    """The device's status word (int32; bit 1: an index outside its tensor was skipped, bit 2: a bounded wait
+    gave up). Kernels OR into it; it is never cleared by them."""
+    index = torch.device("cuda", torch.cuda.current_device() if device is None else
+                         (device if isinstance(device, int) else torch.device(device).index or 0)).index
+    word = _status.get(index)
+    if word is None:
+        word = _status[index] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+    return word
+
+
+def read_status(device=None, clear: bool = True) -> int:
+    """Synchronises, returns the status word and clears it."""
+    word = status_word(device)
+    value = int(word.item())
+    if clear:
+        word.zero_()
+    return value
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dtype(t: torch.Tensor, name: str) -> int:
+    code = _DTYPES.get(t.dtype)
+    if code is None:
+        raise ValueError(f"{name}: dtype {t.dtype} (supported: bfloat16, float32)")
+    return code
+
+
+def _index(t: torch.Tensor) -> torch.Tensor:
+    """int64, contiguous (the reference's index tensors are torch.long)."""
+    if t.dtype != torch.int64:
+        t = t.to(torch.int64)
+    return t.contiguous()
+
+
+def _cache(k: torch.Tensor, v: torch.Tensor, name: str) -> tuple:
+    if k.dim() != 4 or v.shape != k.shape or v.stride() != k.stride():
+        raise ValueError(f"{name}: k and v caches must be [rows, H, S, D] views with the same strides")
+    if k.stride(3) != 1:
+        raise ValueError(f"{name}: cache head_dim stride must be 1")
+    if v.dtype != k.dtype:
+        raise ValueError(f"{name}: k / v dtypes differ")
+    return k.size(0), k.size(2), k.stride(0), k.stride(1), k.stride(2)
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def rope_kv(qkv: torch.Tensor, cs: torch.Tensor, pos: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+            heads: int, slots: torch.Tensor | None = None, cache_pos: torch.Tensor | None = None) -> torch.Tensor:
+    """``qkv`` [N, 3*H*D] (q|k|v of N tokens), ``cs`` [P, D/2, 2] fp32, ``pos`` [N]; ``k_cache``/``v_cache``
+    [rows, H, S, D] with unit stride in D. Rotates at ``pos[n]`` and writes token n's k, v at cache row
+    ``slots[n]`` (default n), position ``cache_pos[n]`` (default ``pos[n]``); returns the rotated q [N, H, D]."""
+    n = qkv.size(0)
+    dim = qkv.size(1) // (3 * heads)
+    q = torch.empty(n, heads, dim, device=qkv.device, dtype=qkv.dtype)
+    if n == 0:
+        return q
+    if qkv.stride(1) != 1:
+        raise ValueError("rope_kv: qkv must have unit inner stride")
+    if k_cache.dtype != qkv.dtype:
+        raise ValueError("rope_kv: cache dtype differs from qkv")
+    cs = cs if cs.dtype == torch.float32 and cs.is_contiguous() else cs.float().contiguous()
+    rows, length, s_row, s_head, s_pos = _cache(k_cache, v_cache, "rope_kv")
+    pos = _index(pos)
+    slots = None if slots is None else _index(slots)
+    cache_pos = None if cache_pos is None else _index(cache_pos)
+    _lib.call("omniasr_rope_kv", _ptr(qkv), qkv.stride(0), _ptr(cs), cs.size(0), _ptr(pos), _ptr(slots),
+              _ptr(cache_pos), _ptr(q), _ptr(k_cache), _ptr(v_cache), rows, length, s_row, s_head, s_pos, n, heads,
+              dim, _dtype(qkv, "rope_kv"), _ptr(status_word(qkv.device)), _stream(qkv.device))
+    return q
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor,
+                     keys: int, scale: float, block: int | None = None, warps: int | None = None,
+                     stages: int | None = None, programs: int | None = None) -> torch.Tensor:
+    """``q`` [B, H, D]; ``k_cache``/``v_cache`` [>=B, H, S, D]; row r attends to keys [0, lengths[r]) (all
+    within the first ``keys``, which fixes the launch grid). Returns [B, H, D] in q's dtype; a row of length 0
+    gets zeros. ``block``/``warps``/``stages``/``programs`` are accepted for API compatibility and ignored."""
+    b, heads, dim = q.shape
+    out = torch.empty_like(q)
+    if b == 0:
+        return out
+    if not q.is_contiguous():
+        raise ValueError("decode_attention: q must be contiguous [B, H, D]")
+    dtype = _dtype(q, "decode_attention")
+    rows, length, s_row, s_head, s_pos = _cache(k_cache, v_cache, "decode_attention")
+    lengths = _index(lengths)
+    lib = _lib.load()
+    nbytes = lib.omniasr_attention_workspace(_lib.DECODE, dtype, b, 1, heads, dim, keys, 0)
+    ws = _workspace(nbytes, q.device)
+    _lib.call("omniasr_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), rows, length, s_row, s_head, s_pos,
+              _ptr(lengths), _ptr(out), b, heads, dim, int(keys), float(scale), dtype, _ptr(ws), ws.numel(),
+              _ptr(status_word(q.device)), _stream(q.device))
+    return out
+
+
+def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor,
+                    tokens: int, keys: int, scale: float, **launch) -> torch.Tensor:
+    """Draft verification: ``q`` [B*T, H, D], row b's T queries at rows b*T .. b*T+T-1; query i of row b attends
+    to keys [0, lengths[b] + i) of cache row b (``k_cache``/``v_cache`` [>=B, H, S, D], all within the first
+    ``keys``). Returns [B*T, H, D] in q's dtype. ``launch`` (reference launch knobs) is ignored."""
+    rows_q, heads, dim = q.shape
+    out = torch.empty_like(q)
+    if rows_q == 0:
+        return out
+    if rows_q % tokens:
+        raise ValueError(f"draft_attention: {rows_q} query rows is not a multiple of tokens={tokens}")
+    if not q.is_contiguous():
+        raise ValueError("draft_attention: q must be contiguous [B*T, H, D]")
+    b = rows_q // tokens
+    dtype = _dtype(q, "draft_attention")
+    rows, length, s_row, s_head, s_pos = _cache(k_cache, v_cache, "draft_attention")
+    lengths = _index(lengths)
+    lib = _lib.load()
+    nbytes = lib.omniasr_attention_workspace(_lib.DRAFT, dtype, b, tokens, heads, dim, keys, 0)
+    ws = _workspace(nbytes, q.device)
+    _lib.call("omniasr_draft_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), rows, length, s_row, s_head, s_pos,
+              _ptr(lengths), _ptr(out), b, int(tokens), heads, dim, int(keys), float(scale), dtype, _ptr(ws),
+              ws.numel(), _ptr(status_word(q.device)), _stream(q.device))
+    return out
+
+
+def beam_attention(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, ctx_len: torch.Tensor, kg: torch.Tensor,
+                   vg: torch.Tensor, ptr: torch.Tensor, gen_len: torch.Tensor, beams: int, ctx_keys: int,
+                   scale: float) -> torch.Tensor:
+    """Beam rows ``q`` [S*N, H, D] (input g's beams are rows g*N .. g*N+N-1): attention over input g's context
+    ``kc``/``vc`` [>=S, H, C, D] (first ``ctx_len[g]`` keys, all within ``ctx_keys``) and row r's generated keys
+    ``kg``/``vg`` [>=S*N, H, G, D], position j taken from row ``ptr[r, j]`` (first ``gen_len[r]``)."""
+    rows_q, heads, dim = q.shape
+    out = torch.empty_like(q)
+    if rows_q == 0:
+        return out
+    if rows_q % beams:
+        raise ValueError(f"beam_attention: {rows_q} rows is not a multiple of beams={beams}")
+    if not q.is_contiguous():
+        raise ValueError("beam_attention: q must be contiguous [S*N, H, D]")
+    if ptr.dtype != torch.int32 or ptr.dim() != 2 or ptr.stride(1) != 1:
+        raise ValueError("beam_attention: ptr must be int32 [R, G] with unit inner stride")
+    groups = rows_q // beams
+    dtype = _dtype(q, "beam_attention")
+    c_rows, c_len, c_row, c_head, c_pos = _cache(kc, vc, "beam_attention")
+    g_rows, g_len, g_row, g_head, g_pos = _cache(kg, vg, "beam_attention")
+    if ptr.size(0) < rows_q or ptr.size(1) < g_len:
+        raise ValueError("beam_attention: ptr must cover [rows, generated length]")
+    ctx_len, gen_len = _index(ctx_len), _index(gen_len)
+    lib = _lib.load()
+    nbytes = lib.omniasr_attention_workspace(_lib.BEAM, dtype, groups, beams, heads, dim, ctx_keys, g_len)
+    ws = _workspace(nbytes, q.device)
+    _lib.call("omniasr_beam_attention", _ptr(q), _ptr(kc), _ptr(vc), c_rows, c_len, c_row, c_head, c_pos,
+              _ptr(ctx_len), _ptr(kg), _ptr(vg), g_rows, g_len, g_row, g_head, g_pos, _ptr(ptr), ptr.stride(0),
+              _ptr(gen_len), _ptr(out), groups, int(beams), heads, dim, int(ctx_keys), float(scale), dtype, _ptr(ws),
+              ws.numel(), _ptr(status_word(q.device)), _stream(q.device))
+    return out
+
+
+def reorder_gather(src: torch.Tensor, parent: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[r] = src[parent[r]]`` along dim 0, byte-exact (``torch.index_select(src, 0, parent)``); each row of
+    ``src`` / ``out`` must be contiguous. ``out`` (optional) must not overlap ``src``."""
+    rows = parent.numel()
+    if out is None:
+        out = torch.empty((rows,) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    if rows == 0:
+        return out
+    if out.shape[1:] != src.shape[1:] or out.size(0) < rows or out.dtype != src.dtype:
+        raise ValueError("reorder_gather: out must be [len(parent), *src.shape[1:]] of src's dtype")
+    if not (src[0].is_contiguous() and out[0].is_contiguous()):
+        raise ValueError("reorder_gather: rows of src and out must be contiguous")
+    if parent.dtype not in (torch.int32, torch.int64):
+        raise ValueError("reorder_gather: parent must be int32 or int64")
+    parent = parent.contiguous()
+    row_bytes = src[0].numel() * src.element_size()
+    _lib.call("omniasr_reorder_gather", _ptr(src), src.stride(0) * src.element_size(), src.size(0), _ptr(out),
+              out.stride(0) * out.element_size(), _ptr(parent), int(parent.dtype == torch.int64), rows, row_bytes,
+              _ptr(status_word(src.device)), _stream(src.device))
+    return out
+
+
+def splits_for(rows: int, heads: int, keys: int, block: int = 64, programs: int = 264) -> tuple[int, int]:
+    """Key splits (a power of two, about ``programs`` programs in all) and the keys each split covers -- the
+    reference's rule (``kernels.py:393-400``), kept for its scripts; these kernels plan their own splits."""
+    s, c = ctypes.c_int(), ctypes.c_int()
+    _lib.call("omniasr_splits_for", int(rows), int(heads), int(keys), int(block), int(programs), ctypes.byref(s),
+              ctypes.byref(c))
+    return s.value, c.value

@@ -1,0 +1,100 @@
+"""The CPU oracle against the golden vectors produced by the reference's own code (tests/golden/make_golden.py)."""
+
+import numpy as np
+import pytest
+import torch
+
+import inputs as gi
+from oracle import attention, bf16, gather, rope, splits
+
+
+def test_bf16_conversion_matches_torch():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100000, dtype=np.float32) * 10.0 ** rng.integers(-30, 30, 100000),
+                        np.array([0.0, -0.0, np.inf, -np.inf, 1e-45, 3.3895314e38, 65504.0], dtype=np.float32)])
+    x = x.astype(np.float32)
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+    assert np.array_equal(bf16.from_float32(x), want)
+    ties = (np.arange(1000, dtype=np.uint32) << 16 | 0x8000).view(np.float32)  # exact halfway cases
+    want = torch.from_numpy(ties).to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+    assert np.array_equal(bf16.from_float32(ties), want)
+    nan = np.array([np.nan], dtype=np.float32)
+    assert np.isnan(bf16.to_float32(bf16.from_float32(nan)))[0]
+
+
+@pytest.mark.parametrize("name", ["rope_bf16_h4_d128", "rope_f32_h4_d128", "rope_bf16_h2_d512", "rope_f32_h2_d16"])
+def test_rope_oracle_bit_exact(golden, name):
+    g = golden(name)
+    is_bf16 = bool(g["is_bf16"])
+    h, d = int(g["heads"]), g["qkv"].shape[1] // (3 * int(g["heads"]))
+    dt = np.uint16 if is_bf16 else np.float32
+    for slots, cpos in ((None, None), (g["slots"], None), (g["slots"], g["cache_pos"])):
+        kc = np.zeros((int(g["rows"]), h, int(g["cache_len"]), d), dtype=dt)
+        vc = np.zeros_like(kc)
+        q = rope.rope_kv(g["qkv"], g["cs"], g["pos"], kc, vc, h, slots, cpos, is_bf16)
+        assert np.array_equal(q.view(np.uint32 if not is_bf16 else np.uint16),
+                              g["q"].view(np.uint32 if not is_bf16 else np.uint16))
+        rows = np.arange(len(g["pos"])) if slots is None else slots
+        at = g["pos"] if cpos is None else cpos
+        assert np.array_equal(kc[rows, :, at], g["k"])
+        assert np.array_equal(vc[rows, :, at], g["v"])
+
+
+def test_gather_oracle(golden):
+    g = golden("gather")
+    assert np.array_equal(gather.reorder_gather(g["ptr"], g["parent"]), g["ptr_out"])
+    assert np.array_equal(gather.reorder_gather(g["hist"], g["parent"]), g["hist_out"])
+    assert np.array_equal(gather.reorder_gather(g["kv"], g["parent"]), g["kv_out"])
+    with pytest.raises(IndexError):
+        gather.reorder_gather(g["ptr"], np.array([0, 6]))
+
+
+def test_splits_oracle(golden):
+    for rows, heads, keys, block, programs, s, c in golden("splits")["cases"]:
+        assert splits.splits_for(int(rows), int(heads), int(keys), int(block), int(programs)) == (s, c)
+
+
+def _t(a, is_bf16):
+    return torch.from_numpy(gi.values(a, is_bf16))
+
+
+@pytest.mark.parametrize("is_bf16", [True, False])
+def test_decode_oracle(golden, is_bf16):
+    g = golden("decode_bf16" if is_bf16 else "decode_f32")
+    q, k, v, lengths = gi.decode_inputs(is_bf16)
+    assert gi.digest(q, k, v, lengths) == str(g["digest"])
+    out = attention.decode_attention(_t(q, is_bf16), _t(k, is_bf16), _t(v, is_bf16), torch.from_numpy(lengths),
+                                     float(g["scale"]))
+    np.testing.assert_allclose(out.numpy(), g["out"], atol=1e-12, rtol=0)
+
+
+@pytest.mark.parametrize("is_bf16", [True, False])
+def test_draft_oracle(golden, is_bf16):
+    g = golden("draft_bf16" if is_bf16 else "draft_f32")
+    q, k, v, lengths = gi.draft_inputs(is_bf16)
+    assert gi.digest(q, k, v, lengths) == str(g["digest"])
+    out = attention.draft_attention(_t(q, is_bf16), _t(k, is_bf16), _t(v, is_bf16), torch.from_numpy(lengths),
+                                    gi.DRAFT["t"], float(g["scale"]))
+    np.testing.assert_allclose(out.numpy(), g["out"], atol=1e-12, rtol=0)
+
+
+@pytest.mark.parametrize("is_bf16", [True, False])
+def test_beam_oracle(golden, is_bf16):
+    g = golden("beam_bf16" if is_bf16 else "beam_f32")
+    q, kc, vc, ctx_len, kg, vg, ptr, gen_len = gi.beam_inputs(is_bf16)
+    assert gi.digest(q, kc, vc, ctx_len, kg, vg, ptr, gen_len) == str(g["digest"])
+    out = attention.beam_attention(_t(q, is_bf16), _t(kc, is_bf16), _t(vc, is_bf16), torch.from_numpy(ctx_len),
+                                   _t(kg, is_bf16), _t(vg, is_bf16), torch.from_numpy(ptr),
+                                   torch.from_numpy(gen_len), gi.BEAM["beams"], float(g["scale"]))
+    # The reference's branch computes its scores in float32 (beam.py:230 `.float()`), the oracle in float64.
+    np.testing.assert_allclose(out.numpy(), g["out"], atol=2e-6, rtol=0)
+    assert np.all(g["out"][-gi.BEAM["beams"]:] == 0)  # the finished input: no keys, zeros
+
+
+def test_oracle_catches_a_planted_error(golden):
+    """A wrong oracle (one key too many per row) must disagree with the reference's vectors."""
+    g = golden("decode_f32")
+    q, k, v, lengths = gi.decode_inputs(False)
+    wrong = attention.decode_attention(_t(q, False), _t(k, False), _t(v, False), torch.from_numpy(lengths) + 1,
+                                       float(g["scale"]))
+    assert np.abs(wrong.numpy() - g["out"]).max() > 1e-3
