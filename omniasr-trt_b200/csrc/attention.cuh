@@ -12,6 +12,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 namespace omni {
@@ -55,6 +56,30 @@ cudaError_t launch_split(int dtype, int dim, bool gather, const SplitPlan& plan,
                          cudaStream_t stream);
 cudaError_t launch_combine(int dtype, int dim, const float* part_o, const float* part_ml, void* out,
                            int64_t rows_heads, int st, cudaStream_t stream);
+
+// Tensor-core pass (bf16, head_dim 128, 1..16 queries per group): persistent stream-K split, see attention_tc.cu.
+struct TcParams {
+  const __nv_bfloat16* q;  // [groups * nq, heads, 128]
+  const int64_t* lengths;  // [groups]
+  int groups, nq, causal, heads;
+  int64_t cap;    // min(cache length, keys): keys a unit may read (set by launch_tc_pass)
+  float qscale;   // softmax scale * log2(e)
+  float* part_o;  // [groups * nq, heads, st, 128]
+  float* part_ml; // [groups * nq, heads, st, 2]
+  int st;         // segments per (row, head) (set by launch_tc_pass)
+  int grid;       // CTAs of the pass (set by launch_tc_pass)
+  __nv_bfloat16* out;  // [groups * nq, heads, 128]: units a single CTA finishes are written here directly
+                       // (null: every unit goes through the combine, e.g. when a second pass adds partials)
+  int* status;
+};
+
+bool tc_path_enabled(int dtype, int dim, int nq);
+int tc_segments(int64_t keys);
+cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
+                           int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream);
+// Merges the pass's segments (plus, for beam search, `extra_st` splits of a second partial region) into out.
+cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o, const float* extra_ml, int extra_st,
+                              cudaStream_t stream);
 
 bool dim_supported(int dtype, int dim);
 int device_sm_count();

@@ -71,12 +71,6 @@ int check_cache(const char* name, const void* k, const void* v, int64_t rows, in
   return OMNIASR_OK;
 }
 
-// One split pass + combine over `groups` groups of `nq` queries.
-struct AttnPass {
-  omni::SplitPlan plan;
-  int st;
-};
-
 }  // namespace
 
 extern "C" {
@@ -114,12 +108,17 @@ size_t omniasr_attention_workspace(int kind, int dtype, int groups, int per_grou
                                    int64_t gen_keys) {
   if (groups <= 0 || per_group <= 0 || heads <= 0 || !omni::dim_supported(dtype, dim)) return 0;
   const int64_t rows_q = (int64_t)groups * per_group;
+  const int nq = kind == OMNIASR_DECODE ? 1 : per_group;
   if (kind == OMNIASR_BEAM) {
-    const omni::SplitPlan c = omni::plan_split(dtype, dim, groups, heads, per_group, keys);
     const omni::SplitPlan g = omni::plan_split(dtype, dim, (int)rows_q, heads, 1, gen_keys);
+    if (omni::tc_path_enabled(dtype, dim, nq))
+      return omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim) +
+             omni::partial_bytes(rows_q, heads, g.splits, dim);
+    const omni::SplitPlan c = omni::plan_split(dtype, dim, groups, heads, per_group, keys);
     return omni::partial_bytes(rows_q, heads, c.splits + g.splits, dim);
   }
-  const omni::SplitPlan p = omni::plan_split(dtype, dim, groups, heads, kind == OMNIASR_DRAFT ? per_group : 1, keys);
+  if (omni::tc_path_enabled(dtype, dim, nq)) return omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
+  const omni::SplitPlan p = omni::plan_split(dtype, dim, groups, heads, nq, keys);
   return omni::partial_bytes(rows_q, heads, p.splits, dim);
 }
 
@@ -176,8 +175,30 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
                                        (long long)cache_rows);
   if (keys < 0 || keys > cache_len)
     return fail(OMNIASR_ERR_ARGUMENT, "%s: keys %d outside [0, cache length %lld]", name, keys, (long long)cache_len);
-  const omni::SplitPlan plan = omni::plan_split(dtype, dim, groups, heads, nq, keys);
   const int64_t rows_q = (int64_t)groups * nq;
+  if (omni::tc_path_enabled(dtype, dim, nq)) {
+    const size_t need = omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
+                  workspace ? workspace_bytes : (size_t)0, need);
+    omni::TcParams t{};
+    t.q = static_cast<const __nv_bfloat16*>(q);
+    t.lengths = lengths;
+    t.groups = groups;
+    t.nq = nq;
+    t.causal = causal;
+    t.heads = heads;
+    t.qscale = scale * omni::kLog2e;
+    t.status = status;
+    t.out = static_cast<__nv_bfloat16*>(out);
+    omni::carve_partials(workspace, rows_q, heads, omni::tc_segments(keys), dim, &t.part_o, &t.part_ml);
+    if (int e = cuda_status(omni::launch_tc_pass(k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                                                 stride_pos, keys, t, stream),
+                            "tensor-core attention launch"))
+      return e;
+    return cuda_status(omni::launch_tc_combine(t, out, nullptr, nullptr, 0, stream), "combine launch");
+  }
+  const omni::SplitPlan plan = omni::plan_split(dtype, dim, groups, heads, nq, keys);
   const size_t need = omni::partial_bytes(rows_q, heads, plan.splits, dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
@@ -258,8 +279,61 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
     return fail(OMNIASR_ERR_ARGUMENT, "%s: ctx_keys %d outside [0, %lld]", name, ctx_keys, (long long)ctx_len_cap);
   if (ptr_stride < gen_len_cap) return fail(OMNIASR_ERR_ARGUMENT, "%s: ptr row stride %lld < generated length %lld",
                                             name, (long long)ptr_stride, (long long)gen_len_cap);
-  const omni::SplitPlan pc = omni::plan_split(dtype, dim, groups, heads, beams, ctx_keys);
   const omni::SplitPlan pg = omni::plan_split(dtype, dim, (int)rows, heads, 1, gen_len_cap);
+  omni::SplitArgs b{};
+  b.q = q;
+  b.k = kg;
+  b.v = vg;
+  b.s_kb = gen_stride_row;
+  b.s_kh = gen_stride_head;
+  b.s_ks = gen_stride_pos;
+  b.cache_rows = gen_rows;
+  b.cache_len = gen_len_cap;
+  b.lengths = gen_len;
+  b.ptr = ptr;
+  b.ptr_stride = ptr_stride;
+  b.heads = heads;
+  b.nq = 1;
+  b.causal = 0;
+  b.chunk = pg.chunk;
+  b.qblocks = 1;
+  b.key_bound = (int64_t)pg.splits * pg.chunk;
+  b.qscale = scale * omni::kLog2e;
+  b.status = status;
+  if (omni::tc_path_enabled(dtype, dim, beams)) {
+    // Context keys on the tensor cores (one read per input for all its beams), generated keys gathered through
+    // the pointers on CUDA cores, one combine over both.
+    const int stc = omni::tc_segments(ctx_keys);
+    const size_t need_c = omni::partial_bytes(rows, heads, stc, dim);
+    const size_t need = need_c + omni::partial_bytes(rows, heads, pg.splits, dim);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
+                  workspace ? workspace_bytes : (size_t)0, need);
+    omni::TcParams t{};
+    t.q = static_cast<const __nv_bfloat16*>(q);
+    t.lengths = ctx_len;
+    t.groups = groups;
+    t.nq = beams;
+    t.causal = 0;
+    t.heads = heads;
+    t.qscale = scale * omni::kLog2e;
+    t.status = status;
+    omni::carve_partials(workspace, rows, heads, stc, dim, &t.part_o, &t.part_ml);
+    float *go, *gml;
+    omni::carve_partials(static_cast<char*>(workspace) + need_c, rows, heads, pg.splits, dim, &go, &gml);
+    if (int e = cuda_status(omni::launch_tc_pass(kc, vc, ctx_rows, ctx_len_cap, ctx_stride_row, ctx_stride_head,
+                                                 ctx_stride_pos, ctx_keys, t, stream),
+                            "context attention launch"))
+      return e;
+    b.part_o = go;
+    b.part_ml = gml;
+    b.st = pg.splits;
+    b.sp_offset = 0;
+    if (int e = cuda_status(omni::launch_split(dtype, dim, true, pg, b, (int)rows, stream), "generated split launch"))
+      return e;
+    return cuda_status(omni::launch_tc_combine(t, out, go, gml, pg.splits, stream), "combine launch");
+  }
+  const omni::SplitPlan pc = omni::plan_split(dtype, dim, groups, heads, beams, ctx_keys);
   const int st = pc.splits + pg.splits;
   const size_t need = omni::partial_bytes(rows, heads, st, dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
@@ -291,22 +365,10 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
   a.status = status;
   if (int e = cuda_status(omni::launch_split(dtype, dim, false, pc, a, groups, stream), "context split launch"))
     return e;
-  omni::SplitArgs b = a;
-  b.k = kg;
-  b.v = vg;
-  b.s_kb = gen_stride_row;
-  b.s_kh = gen_stride_head;
-  b.s_ks = gen_stride_pos;
-  b.cache_rows = gen_rows;
-  b.cache_len = gen_len_cap;
-  b.lengths = gen_len;
-  b.ptr = ptr;
-  b.ptr_stride = ptr_stride;
+  b.part_o = po;
+  b.part_ml = pml;
+  b.st = st;
   b.sp_offset = pc.splits;
-  b.nq = 1;
-  b.chunk = pg.chunk;
-  b.qblocks = 1;
-  b.key_bound = (int64_t)pg.splits * pg.chunk;
   if (int e = cuda_status(omni::launch_split(dtype, dim, true, pg, b, (int)rows, stream), "generated split launch"))
     return e;
   return cuda_status(omni::launch_combine(dtype, dim, po, pml, out, rows * heads, st, stream), "combine launch");

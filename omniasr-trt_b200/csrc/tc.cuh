@@ -1,0 +1,101 @@
+// Blackwell (sm_100a) tensor-core helpers: TMA tensor loads, shared-memory matrix descriptors,
+// tcgen05.mma (kind::f16, one CTA), TMEM allocation and loads, and the fences between them.
+//
+// Descriptor formats follow the PTX ISA's tcgen05 "shared memory descriptor" and "instruction
+// descriptor" tables (the same fields CUTLASS names UMMA::SmemDescriptor / InstrDescriptor).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace omni {
+
+// ---- TMA (tiled tensor) ----------------------------------------------------------------------
+
+OMNI_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 4-D tiled load into this CTA's shared memory (no multicast), completion on `bar`.
+OMNI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// ---- descriptors -----------------------------------------------------------------------------
+
+constexpr uint32_t kLayoutNone = 0;   // no swizzle: 8-row x 16-byte core matrices
+constexpr uint32_t kLayoutSw128 = 2;  // 128-byte swizzle (the TMA's CU_TENSOR_MAP_SWIZZLE_128B)
+
+// Shared-memory matrix descriptor: start address, leading / stride byte offsets (bytes), layout.
+OMNI_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// kind::f16 instruction descriptor: bf16 A and B, fp32 accumulator, M x N, K-major (0) or
+// MN-major (1) operands.
+constexpr uint32_t idesc_bf16(int m, int n, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) | ((uint32_t)b_mn_major << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---- tcgen05 ---------------------------------------------------------------------------------
+
+// D (TMEM) = A (smem) x B (smem) [+ D]; issued by one thread.
+OMNI_DEV void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation this thread issued before has completed.
+OMNI_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+OMNI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+OMNI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes -> visible to the tensor core / TMA (async proxy).
+OMNI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Warp-wide: allocate `ncols` TMEM columns (power of two >= 32); the base address goes to *dst.
+OMNI_DEV void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+OMNI_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Warp-wide: 16 consecutive fp32 columns of this thread's TMEM lane (lane = 32 * (warp % 4) + laneid).
+OMNI_DEV void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Named barrier over `count` threads (id 1..15; 0 is __syncthreads).
+OMNI_DEV void named_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+
+}  // namespace omni

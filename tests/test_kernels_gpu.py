@@ -382,3 +382,38 @@ def test_reorder_gather_rejects_overlap_and_flags_bad_parent(K):
     out = K.reorder_gather(src, torch.tensor([1, 8, 0], device="cuda"))
     assert K.read_status() & 1
     assert torch.equal(out[0], src[1]) and torch.equal(out[2], src[0])
+
+
+@pytest.mark.parametrize("tokens", [1, 2, 3, 4, 6, 8, 9, 16])
+def test_draft_attention_every_query_count_d128(K, tokens):
+    """bf16 head_dim 128 runs on the tensor cores for 1..16 queries per row: every compile-time width, ragged lengths
+    (units cut between CTAs and partial last tiles), finished rows (length 0)."""
+    b, h, d, cap = 6, 16, 128, 3000
+    g = torch.Generator().manual_seed(100 + tokens)
+    lengths = torch.randint(1, 2800 - tokens, (b,), generator=g)
+    lengths[1] = 0
+    lengths[2] = 128 - tokens + 1  # the last query ends exactly on a tile boundary
+    kc = randn((b, h, cap, d), torch.bfloat16, 110)
+    vc = randn((b, h, cap, d), torch.bfloat16, 111)
+    q = randn((b * tokens, h, d), torch.bfloat16, 112)
+    keys = int((lengths.max() + tokens + 255) // 256 * 256)
+    out = K.draft_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), tokens, min(keys, cap), d**-0.5)
+    want = oatt.draft_attention(q, kc, vc, lengths, tokens, d**-0.5)
+    check_attention(out, want, torch.bfloat16, what=f"draft T={tokens}")
+    assert K.read_status() == 0
+
+
+def test_tc_attention_uninitialised_cache_tail_is_ignored(K):
+    """Keys past a row's length may hold anything (NaN here): they must not reach the output."""
+    b, h, d, cap = 3, 4, 128, 700
+    kc = randn((b, h, cap, d), torch.bfloat16, 120)
+    vc = randn((b, h, cap, d), torch.bfloat16, 121)
+    lengths = torch.tensor([300, 129, 1])
+    for r in range(b):
+        kc[r, :, int(lengths[r]):] = float("nan")
+        vc[r, :, int(lengths[r]):] = float("nan")
+    q = randn((b, h, d), torch.bfloat16, 122)
+    out = K.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), cap, d**-0.5)
+    assert not torch.isnan(out).any()
+    kz, vz = kc.nan_to_num(0.0), vc.nan_to_num(0.0)
+    check_attention(out, oatt.decode_attention(q, kz, vz, lengths, d**-0.5), torch.bfloat16, what="nan tail")
