@@ -68,6 +68,8 @@ struct TcParams {
   float* part_ml; // [groups * nq, heads, st, 2]
   int st;         // segments per (row, head) (set by launch_tc_pass)
   int grid;       // CTAs of the pass (set by launch_tc_pass)
+  int unit_cost;  // scheduling cost of a unit's start, in eighths of a tile (set by launch_tc_pass)
+  int prefetch;   // tiles prefetched into L2 ahead of the loads (set by launch_tc_pass)
   __nv_bfloat16* out;  // [groups * nq, heads, 128]: units a single CTA finishes are written here directly
                        // (null: every unit goes through the combine, e.g. when a second pass adds partials)
   int* status;

@@ -24,6 +24,32 @@
 #include "attention.cuh"
 #include "tc.cuh"
 
+// Per-tile timeline hook for development builds: -DOMNI_TRACE records clock64() of CTA 0's pipeline events into
+// omni_trace[] (read back by the tracing harness). Product builds compile it to nothing.
+#ifdef OMNI_TRACE
+__device__ unsigned long long omni_trace[4096];
+#define OMNI_TRACE_AT(slot)                                    \
+  do {                                                         \
+    if (blockIdx.x == 0 && (slot) < 4096) omni_trace[(slot)] = clock64(); \
+  } while (0)
+// Start / end (global timer, ns) of every CTA at omni_trace[2048 + 2 * cta].
+#define OMNI_TRACE_CTA(which)                                                            \
+  do {                                                                                   \
+    if (threadIdx.x == 0 && blockIdx.x < 1000) {                                         \
+      unsigned long long t_;                                                             \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                            \
+      omni_trace[2048 + 2 * blockIdx.x + (which)] = t_;                                 \
+    }                                                                                    \
+  } while (0)
+#else
+#define OMNI_TRACE_AT(slot) \
+  do {                      \
+  } while (0)
+#define OMNI_TRACE_CTA(which) \
+  do {                        \
+  } while (0)
+#endif
+
 namespace omni {
 
 namespace tcattn {
@@ -31,14 +57,19 @@ namespace tcattn {
 constexpr int D = 128;
 constexpr int BN = 128;          // keys per tile (the MMA's M)
 constexpr int NQP = 16;          // query columns (the MMA's N)
-constexpr int SLOTS = 6;         // ring slots: K and V of 3 tiles
-constexpr int SLOT_BYTES = BN * D * 2;
+constexpr int SLOT_BYTES = BN * D * 2;  // one K or V tile
 constexpr int BOX_BYTES = BN * 64 * 2;  // one 64-column box of a tile
-constexpr int Q_OFF = SLOTS * SLOT_BYTES;
-constexpr int P_OFF = Q_OFF + NQP * D * 2;
-constexpr int RED_OFF = P_OFF + 2 * NQP * BN * 2;
-constexpr int SMEM_BYTES = RED_OFF + 4 * NQP * 4 + 1024;  // + alignment slack
-constexpr int THREADS = 160;
+
+// Shared-memory layout of a CTA with SLOTS tile slots: K of tile i in slot i % (SLOTS / 2), V in slot
+// SLOTS / 2 + i % (SLOTS / 2), so K loads never wait behind V loads (each has its own producer).
+template <int SLOTS>
+struct Smem {
+  static constexpr int Q_OFF = SLOTS * SLOT_BYTES;      // two query buffers (units u and u + 1), 4 KB each
+  static constexpr int P_OFF = Q_OFF + 2 * NQP * D * 2;
+  static constexpr int RED_OFF = P_OFF + 2 * NQP * BN * 2;
+  static constexpr int BYTES = RED_OFF + 4 * NQP * 4 + 1024;  // + alignment slack
+};
+constexpr int THREADS = 224;  // warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads
 constexpr uint32_t TMEM_COLS = 64;  // S^T x2 (cols 0-31), O^T x2 (cols 32-63)
 constexpr uint32_t IDESC_S = idesc_bf16(128, NQP, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(128, NQP, 1, 1);
@@ -52,39 +83,89 @@ OMNI_DEV int64_t unit_need(const Params& p, int g) {
   return n > p.cap ? p.cap : n;
 }
 
-// Walks the global tile sequence (groups outer, heads inner, tiles of a unit innermost).
-struct Walk {
-  int g;
-  int64_t pre;    // first global tile of group g
-  int64_t tiles;  // tiles per unit of group g
-  int64_t need;   // keys per unit of group g
-  OMNI_DEV void start(const Params& p, int64_t x) {
+// Work is split between CTAs by cost, not by tiles: a unit (group, head) costs p.unit_cost for its start and
+// epilogue plus kTileCost per tile, and tile t of unit (g, h) sits at cost position
+//   pre(g) + h * ucost(g) + unit_cost + kTileCost * t,   pre(g) = sum over earlier groups of heads * ucost.
+// CTA b owns the tiles whose position lies in [b * per, (b + 1) * per), per = ceil(total cost / grid).
+constexpr int64_t kTileCost = 8;
+constexpr int kSmemGroups = 256;  // groups whose lengths the pass keeps in shared memory
+
+OMNI_DEV int64_t unit_cost(const Params& p, int64_t tiles) { return tiles > 0 ? p.unit_cost + kTileCost * tiles : 0; }
+
+OMNI_DEV int64_t total_cost(const Params& p) {
+  int64_t c = 0;
+  for (int g = 0; g < p.groups; ++g) c += unit_cost(p, (unit_need(p, g) + BN - 1) / BN) * p.heads;
+  return c;
+}
+
+// The tiles of one CTA, in order (groups outer, heads inner, tiles of a unit innermost).
+struct TileIter {
+  const Params* p;
+  int64_t c1;
+  int g, h, t;
+  int64_t pre, tiles, ucost, need, pos;
+  bool done;
+  OMNI_DEV void load_group() {
+    need = unit_need(*p, g);
+    tiles = (need + BN - 1) / BN;
+    ucost = unit_cost(*p, tiles);
+  }
+  // Skips heads past the last and groups without tiles.
+  OMNI_DEV void normalize() {
+    while (!done && (tiles == 0 || h >= p->heads)) {
+      if (g >= p->groups - 1) {
+        done = true;
+        return;
+      }
+      pre += ucost * p->heads;
+      ++g;
+      load_group();
+      h = 0;
+      t = 0;
+    }
+  }
+  OMNI_DEV void place() {
+    if (done) return;
+    pos = pre + h * ucost + p->unit_cost + kTileCost * t;
+    if (pos >= c1) done = true;
+  }
+  OMNI_DEV void init(const Params& pp, int64_t c0, int64_t c1_) {
+    p = &pp;
+    c1 = c1_;
     g = 0;
     pre = 0;
-    for (;;) {
-      need = unit_need(p, g);
-      tiles = (need + BN - 1) / BN;
-      if (g == p.groups - 1 || x < pre + tiles * p.heads) break;
-      pre += tiles * p.heads;
+    h = t = 0;
+    done = false;
+    load_group();
+    while (g < p->groups - 1 && c0 >= pre + ucost * p->heads) {
+      pre += ucost * p->heads;
       ++g;
+      load_group();
     }
-  }
-  // Moves forward to the group holding global tile x (x never decreases).
-  OMNI_DEV void seek(const Params& p, int64_t x) {
-    while (x >= pre + tiles * p.heads && g < p.groups - 1) {
-      pre += tiles * p.heads;
-      ++g;
-      need = unit_need(p, g);
-      tiles = (need + BN - 1) / BN;
+    if (ucost > 0) {
+      const int64_t r = c0 - pre;
+      h = (int)(r / ucost);
+      const int64_t q = r - h * ucost;
+      t = q <= p->unit_cost ? 0 : (int)((q - p->unit_cost + kTileCost - 1) / kTileCost);
+      if (t >= tiles) {
+        t = 0;
+        ++h;
+      }
     }
+    normalize();
+    place();
   }
+  OMNI_DEV void advance() {
+    if (++t >= tiles) {
+      t = 0;
+      ++h;
+    }
+    normalize();
+    place();
+  }
+  OMNI_DEV bool last_here() const { return t == tiles - 1 || pos + kTileCost >= c1; }
+  OMNI_DEV int64_t unit_pos0() const { return pre + h * ucost + p->unit_cost; }
 };
-
-OMNI_DEV int64_t total_tiles(const Params& p) {
-  int64_t t = 0;
-  for (int g = 0; g < p.groups; ++g) t += (unit_need(p, g) + BN - 1) / BN * p.heads;
-  return t;
-}
 
 OMNI_DEV bool named_sync_and(int id, int count, bool pred) {
   uint32_t out;
@@ -99,7 +180,45 @@ OMNI_DEV bool named_sync_and(int id, int count, bool pred) {
   return out != 0;
 }
 
+// Per-column totals of N values held by each of 32 lanes, in N - 1 + (5 - log2 N) shuffles instead of 5 N:
+// each step a lane keeps half of its columns and adds its partner's copy of them. Returns this lane's column
+// total and sets `col`; lanes whose low 5 - log2 N bits are zero hold distinct columns.
+template <int N, bool MAX>
+OMNI_DEV float butterfly(const float (&v)[N], int lane, int& col) {
+  float w[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) w[i] = v[i];
+  int off = 16;
+  col = 0;
+#pragma unroll
+  for (int step = 0; (1 << step) < N; ++step) {
+    const int half = N >> (step + 1);
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = upper ? w[i] : w[half + i];
+      const float keep = upper ? w[half + i] : w[i];
+      const float got = __shfl_xor_sync(0xffffffffu, send, off);
+      w[i] = MAX ? fmaxf(keep, got) : keep + got;
+    }
+    if (upper) col += half;
+    off >>= 1;
+  }
+  float r = w[0];
+  for (; off > 0; off >>= 1) {
+    const float got = __shfl_xor_sync(0xffffffffu, r, off);
+    r = MAX ? fmaxf(r, got) : r + got;
+  }
+  return r;
+}
+
+template <int N>
+OMNI_DEV bool butterfly_writer(int lane) {
+  return (lane & (32 / N - 1)) == 0;
+}
+
 constexpr float kRescale = 8.f;  // log2 units: probabilities may reach 2^8 before the running max is raised
+constexpr float kBelow = 64.f;   // ... and the first tile's scores may lie 2^64 below the initial guess
 
 OMNI_DEV bool named_sync_or(int id, int count, bool pred) {
   uint32_t out;
@@ -121,7 +240,7 @@ OMNI_DEV void issue_scores(uint32_t tbase, int buf, const unsigned char* kslot, 
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint64_t a = smem_desc(kaddr + (kk >> 2) * BOX_BYTES + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-    const uint64_t b = smem_desc(qaddr + kk * 256, 128, 2048, kLayoutNone);
+    const uint64_t b = smem_desc(qaddr + (kk >> 2) * (NQP * 128) + (kk & 3) * 32, 16, 1024, kLayoutSw128);
     mma_bf16_ss(tbase + buf * NQP, a, b, IDESC_S, kk > 0 ? 1u : 0u);
   }
 }
@@ -138,28 +257,52 @@ OMNI_DEV void issue_values(uint32_t tbase, int buf, const unsigned char* vslot, 
   }
 }
 
-// NQT: query columns processed (a compile-time bound >= nq; the MMA always computes 16).
-template <int NQT>
+// NQT: query columns processed (a compile-time bound >= nq; the MMA always computes 16). SLOTS: ring slots (K and V of
+// SLOTS / 2 tiles in flight; six fill the shared memory of one CTA per SM).
+//
+// Roles and their handshakes (mbarriers; b = tile & 1, u = tile >> 1 its use of buffer b):
+//   producer (warp 4)   full[slot]  <- TMA bytes           empty[slot] -> refill
+//   MMA (warp 5)        s_full[b]   <- S^T(tile) done      o_full[b]   <- O^T(tile) done
+//   softmax (warps 0-3) s_free[b], p_full[b], o_free[b] (128 arrivals each)
+//   queries (TMA by the producer, two buffers by unit parity): q_fill[q] <- bytes, q_done[q] <- unit's last S^T
+template <int NQT, int SLOTS>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap qmap, const Params pin) {
+  using L = Smem<SLOTS>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t full[SLOTS], empty[SLOTS], bar_s[2], bar_o[2], drain;
+  __shared__ __align__(8) uint64_t full[SLOTS], empty[SLOTS];
+  __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_fill[2], q_done[2], drain;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
-  __shared__ volatile int issued_k, issued_v, done_tiles;  // K / V loads issued, tiles fully consumed
+  __shared__ volatile int issued_k, issued_v, q_issued;  // K / V tiles and query tiles the producers issued
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  const int64_t total = total_tiles(p);
-  const int64_t per = total > 0 ? (total + gridDim.x - 1) / gridDim.x : 1;
-  const int64_t x0 = (int64_t)blockIdx.x * per;
-  const int64_t x1 = min(total, x0 + per);
-  if (x0 >= x1) return;  // nothing for this CTA (uniform)
+  // The lengths, read by every role's walk, once into shared memory.
+  __shared__ int64_t s_len[kSmemGroups];
+  Params p = pin;
+  if (p.groups <= kSmemGroups) {
+    for (int g = tid; g < p.groups; g += THREADS) s_len[g] = pin.lengths[g];
+    __syncthreads();
+    p.lengths = s_len;
+  }
+
+  const int64_t total = total_cost(p);
+  // At least one tile's cost per CTA, so that every CTA between a unit's first and last owns one of its tiles.
+  const int64_t per = max((total + gridDim.x - 1) / gridDim.x, kTileCost);
+  const int64_t c0 = (int64_t)blockIdx.x * per;
+  const int64_t c1 = min(total, c0 + per);
+  {
+    TileIter probe;
+    probe.init(p, c0, c1);
+    if (c0 >= c1 || probe.done) return;  // no tile for this CTA (uniform)
+  }
+  OMNI_TRACE_CTA(0);
 
   if (tid == 0) {
     for (int s = 0; s < SLOTS; ++s) {
@@ -167,151 +310,208 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar_s[s], 1);
-      mbar_init(&bar_o[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&o_full[s], 1);
+      mbar_init(&s_free[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_free[s], 128);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_fill[s], 1);
+      mbar_init(&q_done[s], 1);
     }
     mbar_init(&drain, 1);
     mbar_fence_init();
     abort_flag = 0;
-    issued_k = issued_v = done_tiles = 0;
+    issued_k = issued_v = q_issued = 0;
   }
+  if (tid == 0) OMNI_TRACE_AT(4000);
   if (warp == 0) tmem_alloc(&tmem_base, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0) {
+    OMNI_TRACE_AT(4001);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the combine may start its prologue
+  }
   const uint32_t tbase = tmem_base;
+  unsigned char* qs = smem + L::Q_OFF;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------------ producer
+  constexpr int HALF = SLOTS / 2;
+  if (warp == 4 || warp == 6) {
+    // ------------------------------------------------------------------ producers: K (+ queries) and V
     if (lane == 0) {
-      prefetch_tmap(&kmap);
-      prefetch_tmap(&vmap);
-      Walk w;
-      w.start(p, x0);
-      for (int64_t x = x0; x < x1; ++x) {
-        if (abort_flag) break;
-        w.seek(p, x);
-        const int64_t r = x - w.pre;
-        const int h = (int)(r / w.tiles);
-        const int k0 = (int)(r % w.tiles) * BN;
-        const int it = (int)(x - x0);
-        const int ks = 2 * (it % 3), vs = ks + 1;
-        const int use = it / 3;
-        if (use >= 1 && !mbar_wait(&empty[ks], (use - 1) & 1)) {
+      const bool is_k = warp == 4;
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
+      prefetch_tmap(map);
+      if (is_k) prefetch_tmap(&qmap);
+      TileIter ti, ahead;  // `ahead` runs p.prefetch tiles in front: those go to L2 early, beyond the ring
+      ti.init(p, c0, c1);
+      ahead.init(p, c0, c1);
+      for (int i = 0; i < p.prefetch && !ahead.done; ++i) ahead.advance();
+      int unit = 0;
+      for (int it = 0; !ti.done && !abort_flag; ++it, ti.advance()) {
+        const int h = ti.h, tt = ti.t;
+        if (p.prefetch > 0 && !ahead.done) {
+          tma_prefetch_4d(map, 0, ahead.t * BN, ahead.h, ahead.g);
+          tma_prefetch_4d(map, 64, ahead.t * BN, ahead.h, ahead.g);
+          ahead.advance();
+        }
+        if (is_k && (tt == 0 || it == 0)) {
+          // The unit's queries (16 rows of head h from row g * nq; rows past the group are masked later).
+          const int qb = unit & 1;
+          if (unit >= 2 && !mbar_wait(&q_done[qb], ((unit >> 1) - 1) & 1)) {
+            abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_fill[qb], NQP * D * 2);
+          tma_load_3d(qs + qb * (NQP * D * 2), &qmap, 0, h, ti.g * p.nq, &q_fill[qb]);
+          tma_load_3d(qs + qb * (NQP * D * 2) + NQP * 128, &qmap, 64, h, ti.g * p.nq, &q_fill[qb]);
+          q_issued = ++unit;
+        }
+        const int slot = (is_k ? 0 : HALF) + it % HALF, use = it / HALF;
+        if (use >= 1 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
           abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[ks], SLOT_BYTES);
-        tma_load_4d(smem + ks * SLOT_BYTES, &kmap, 0, k0, h, w.g, &full[ks]);
-        tma_load_4d(smem + ks * SLOT_BYTES + BOX_BYTES, &kmap, 64, k0, h, w.g, &full[ks]);
-        issued_k = it + 1;
-        if (use >= 1 && !mbar_wait(&empty[vs], (use - 1) & 1)) {
-          abort_flag = 1;
-          break;
+        mbar_arrive_expect_tx(&full[slot], SLOT_BYTES);
+        tma_load_4d(smem + slot * SLOT_BYTES, map, 0, tt * BN, h, ti.g, &full[slot]);
+        tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, map, 64, tt * BN, h, ti.g, &full[slot]);
+        if (is_k) {
+          issued_k = it + 1;
+          OMNI_TRACE_AT(it * 8);
+        } else {
+          issued_v = it + 1;
+          OMNI_TRACE_AT(it * 8 + 1);
         }
-        mbar_arrive_expect_tx(&full[vs], SLOT_BYTES);
-        tma_load_4d(smem + vs * SLOT_BYTES, &vmap, 0, k0, h, w.g, &full[vs]);
-        tma_load_4d(smem + vs * SLOT_BYTES + BOX_BYTES, &vmap, 64, k0, h, w.g, &full[vs]);
-        issued_v = it + 1;
       }
     }
     __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      TileIter ti;
+      ti.init(p, c0, c1);
+      int unit = -1;
+      auto scores = [&](int t) -> bool {  // S^T(t) = K(t) Q^T
+        const int b = t & 1, u = t >> 1;
+        const int slot = t % HALF;
+        if (u >= 1 && !mbar_wait(&s_free[b], (u - 1) & 1)) return false;
+        if (!mbar_wait(&full[slot], (t / HALF) & 1)) return false;
+        tc_fence_after();
+        OMNI_TRACE_AT(t * 8 + 2);
+        issue_scores(tbase, b, smem + slot * SLOT_BYTES, qs + (unit & 1) * (NQP * D * 2));
+        tc_commit(&s_full[b]);
+        tc_commit(&empty[slot]);
+        return true;
+      };
+      auto values = [&](int t) -> bool {  // O^T(t) = V(t)^T P^T(t)
+        const int b = t & 1, u = t >> 1;
+        const int slot = HALF + t % HALF;
+        if (u >= 1 && !mbar_wait(&o_free[b], (u - 1) & 1)) return false;
+        if (!mbar_wait(&p_full[b], u & 1)) return false;
+        if (!mbar_wait(&full[slot], (t / HALF) & 1)) return false;
+        tc_fence_after();
+        OMNI_TRACE_AT(t * 8 + 3);
+        issue_values(tbase, b, smem + slot * SLOT_BYTES, smem + L::P_OFF + b * (NQP * BN * 2));
+        tc_commit(&o_full[b]);
+        tc_commit(&empty[slot]);
+        return true;
+      };
+      // Within a unit, tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1)
+      // runs; at a unit boundary O^T(t-1) goes first (the softmax needs it to finish the unit).
+      bool ok = true;
+      int pend = -1;  // tile whose O^T is still to issue
+      for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
+        if (ti.t == 0 || it == 0) {
+          if (pend >= 0) {
+            ok = values(pend);
+            pend = -1;
+          }
+          ++unit;
+          if (ok && !mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
+        }
+        if (ok) ok = scores(it);
+        if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
+        if (ok && pend >= 0) ok = values(pend);
+        pend = it;
+      }
+      if (ok && pend >= 0 && !abort_flag) ok = values(pend);
+      if (!ok) abort_flag = 1;
+    }
+    __syncwarp();
   } else {
-    // ------------------------------------------------------------------ consumers (128 threads)
-    // Per tile: S^T (issued one tile ahead) -> softmax (the running max is raised only when a score passes it by
-    // 2^8, so the cross-thread max is rare) -> P^T -> O^T (accumulated one tile later, overlapping the next tile).
+    // ------------------------------------------------------------------ softmax (128 threads, TMEM lane = tid)
+    // The running max of a column is raised only when a score passes it by 2^8, so the cross-thread max (and the
+    // rescale of the accumulators) is rare; O^T of a tile is accumulated one tile later.
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    unsigned char* qs = smem + Q_OFF;
-    float* red = reinterpret_cast<float*>(smem + RED_OFF);
-    Walk w;
-    w.start(p, x0);
+    float* red = reinterpret_cast<float*>(smem + L::RED_OFF);
+    TileIter ti;
+    ti.init(p, c0, c1);
     float m[NQT], lpart[NQT], acc[NQT], scl[NQT];
     int lim[NQT];
-    int g = 0, h = 0;
-    int64_t unit_first = 0;
-    bool pending = false;  // an O^T tile issued and not yet accumulated
-    bool ok_all = true;
-    int it = 0;
-    for (int64_t x = x0; x < x1; ++x, ++it) {
-      w.seek(p, x);
-      const int64_t r = x - w.pre;
-      const int tt = (int)(r % w.tiles);
-      const int buf = it & 1;
-      const int ks = 2 * (it % 3), vs = ks + 1;
-      const uint32_t slot_parity = (it / 3) & 1;
-      const uint32_t buf_parity = (it >> 1) & 1;
-      const bool first = tt == 0 || x == x0;
-      const bool last = tt == w.tiles - 1 || x == x1 - 1;
+    int g = 0, h = 0, need = 0, tiles = 1;
+    int64_t unit_pos0 = 0;
+    bool pending = false;
+    for (int it = 0; !ti.done; ++it, ti.advance()) {
+      const int tt = ti.t;
+      const int b = it & 1;
+      const uint32_t par = (it >> 1) & 1;
+      const bool first = tt == 0 || it == 0;
+      const bool last = ti.last_here();
       if (first) {
-        g = w.g;
-        h = (int)(r / w.tiles);
-        unit_first = w.pre + (int64_t)h * w.tiles;
+        g = ti.g;
+        h = ti.h;
+        tiles = (int)ti.tiles;
+        need = (int)ti.need;
+        unit_pos0 = ti.unit_pos0();
         const int64_t n = p.lengths[g];
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
           int64_t lj = n + (p.causal ? j : 0);
           lj = lj < 0 ? 0 : lj;
-          lim[j] = j < p.nq ? (int)(lj > w.need ? w.need : lj) : 0;
-          m[j] = -INFINITY;
+          lim[j] = j < p.nq ? (int)(lj > need ? need : lj) : 0;
+          m[j] = 0.f;  // a guess; the first tile lowers it if its scores are far below, or raises it
           lpart[j] = 0.f;
           acc[j] = 0.f;
         }
-        for (int i = tid; i < NQP * (D / 8); i += 128) {
-          const int j = i / (D / 8), c = i % (D / 8);
-          uint4 val = make_uint4(0u, 0u, 0u, 0u);
-          if (j < p.nq)
-            val = __ldg(reinterpret_cast<const uint4*>(p.q + (((int64_t)g * p.nq + j) * p.heads + h) * D) + c);
-          *reinterpret_cast<uint4*>(qs + (j >> 3) * 2048 + c * 128 + (j & 7) * 16) = val;
-        }
-        fence_async_smem();
-        __syncwarp();
-        named_sync(1, 128);
-        if (tid == 0) {
-          if (mbar_wait(&full[ks], slot_parity)) {
-            tc_fence_after();
-            issue_scores(tbase, buf, smem + ks * SLOT_BYTES, qs);
-            tc_commit(&bar_s[buf]);
-            tc_commit(&empty[ks]);
-          } else {
-            abort_flag = 1;
-          }
-        }
       }
       const int key = tt * BN + tid;
+      if (tid == 0) OMNI_TRACE_AT(it * 8 + 7);
 
       // Scores of this tile.
-      if (!mbar_wait(&bar_s[buf], buf_parity)) abort_flag = 1;
+      if (!mbar_wait(&s_full[b], par)) abort_flag = 1;
+      if (tid == 0) OMNI_TRACE_AT(it * 8 + 4);
       tc_fence_after();
       __syncwarp();
       float s[NQP];
-      tmem_ld16(tbase + lane_off + buf * NQP, s);
+      tmem_ld16(tbase + lane_off + b * NQP, s);
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
       float xv[NQT];
       bool over = false;
 #pragma unroll
       for (int j = 0; j < NQT; ++j) {
         xv[j] = key < lim[j] ? s[j] * p.qscale : -INFINITY;
         over |= xv[j] > m[j] + kRescale;
+        if (first) over |= xv[j] > -INFINITY && xv[j] < m[j] - kBelow;
       }
-      const bool any_over = named_sync_or(1, 128, over);
-      if (abort_flag) {  // uniform: written before the barrier
-        ok_all = false;
-        break;
-      }
-      if (any_over) {
-        // Raise the running max of every column to this tile's maximum (cross-thread reduction).
-#pragma unroll
-        for (int j = 0; j < NQT; ++j) {
-          float v = xv[j];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-          if (lane == 0) red[warp * NQP + j] = v;
+      // One barrier per tile: does any thread need a new max, or has any seen an abort? (Both take the slow
+      // path, whose barrier then decides the abort from the values each thread read before the first one.)
+      const bool saw_abort = abort_flag != 0;
+      if (named_sync_or(1, 128, over || saw_abort)) {
+        {
+          int col;
+          const float v = butterfly<NQT, true>(xv, lane, col);
+          if (butterfly_writer<NQT>(lane)) red[warp * NQP + col] = v;
         }
-        named_sync(1, 128);
+        if (named_sync_or(1, 128, saw_abort)) break;
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
           const float tmax = fmaxf(fmaxf(red[j], red[NQP + j]), fmaxf(red[2 * NQP + j], red[3 * NQP + j]));
-          const float mnew = fmaxf(m[j], tmax);
-          scl[j] = ex2(m[j] - (mnew == -INFINITY ? 0.f : mnew));  // 0 while the column has seen no key
+          // First tile of the unit here: nothing is accumulated yet, so the max may also go down.
+          const float mnew = first ? (tmax == -INFINITY ? m[j] : tmax) : fmaxf(m[j], tmax);
+          scl[j] = ex2(m[j] - mnew);
           m[j] = mnew;
           acc[j] *= scl[j];
           lpart[j] *= scl[j];
@@ -326,11 +526,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < NQP; ++j) pr[j] = 0.f;
 #pragma unroll
       for (int j = 0; j < NQT; ++j) {
-        pr[j] = ex2(xv[j] - (m[j] == -INFINITY ? 0.f : m[j]));
+        pr[j] = ex2(xv[j] - m[j]);
         lpart[j] += pr[j];
       }
       {
-        unsigned char* pb = smem + P_OFF + buf * (NQP * BN * 2);
+        unsigned char* pb = smem + L::P_OFF + b * (NQP * BN * 2);
         uint32_t wv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -339,15 +539,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           wv[i] = lo | (hi << 16);
         }
         *reinterpret_cast<uint4*>(pb + tid * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        if (NQT > 8) *reinterpret_cast<uint4*>(pb + 2048 + tid * 16) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
-        else *reinterpret_cast<uint4*>(pb + 2048 + tid * 16) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(pb + 2048 + tid * 16) =
+            NQT > 8 ? make_uint4(wv[4], wv[5], wv[6], wv[7]) : make_uint4(0u, 0u, 0u, 0u);
       }
       // A tile that ends inside the unit's keys: zero the V rows past them (they may hold anything).
-      const bool partial = (int64_t)tt * BN + BN > w.need;
-      if (partial) {
-        if (!mbar_wait(&full[vs], slot_parity)) abort_flag = 1;
-        if (key >= w.need) {
-          unsigned char* row = smem + vs * SLOT_BYTES + tid * 128;
+      if (tt * BN + BN > need) {
+        const int vslot = HALF + it % HALF;
+        if (!mbar_wait(&full[vslot], (it / HALF) & 1)) abort_flag = 1;
+        if (key >= need) {
+          unsigned char* row = smem + vslot * SLOT_BYTES + tid * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             *reinterpret_cast<uint4*>(row + c * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -356,66 +556,44 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      named_sync(1, 128);  // P^T (and zeroed V rows) ready
-
-      if (tid == 0) {
-        tc_fence_after();
-        if (partial || mbar_wait(&full[vs], slot_parity)) {
-          issue_values(tbase, buf, smem + vs * SLOT_BYTES, smem + P_OFF + buf * (NQP * BN * 2));
-          tc_commit(&bar_o[buf]);
-          tc_commit(&empty[vs]);
-        } else {
-          abort_flag = 1;
-        }
-        if (!last) {  // the next tile belongs to this unit: its scores now, overlapping this tile's tail
-          const int ks2 = 2 * ((it + 1) % 3);
-          if (mbar_wait(&full[ks2], ((it + 1) / 3) & 1)) {
-            issue_scores(tbase, buf ^ 1, smem + ks2 * SLOT_BYTES, qs);
-            tc_commit(&bar_s[buf ^ 1]);
-            tc_commit(&empty[ks2]);
-          } else {
-            abort_flag = 1;
-          }
-        }
-      }
-      __syncwarp();
+      mbar_arrive(&p_full[b]);
+      if (tid == 0) OMNI_TRACE_AT(it * 8 + 5);
 
       // The previous tile's O^T, brought to this tile's max.
       if (pending) {
-        if (!mbar_wait(&bar_o[buf ^ 1], ((it - 1) >> 1) & 1)) abort_flag = 1;
+        if (!mbar_wait(&o_full[b ^ 1], ((it - 1) >> 1) & 1)) abort_flag = 1;
+        if (tid == 0) OMNI_TRACE_AT(it * 8 + 6);
         tc_fence_after();
         __syncwarp();
         float o[NQP];
-        tmem_ld16(tbase + lane_off + 2 * NQP + (buf ^ 1) * NQP, o);
+        tmem_ld16(tbase + lane_off + 2 * NQP + (b ^ 1) * NQP, o);
+        tc_fence_before();
+        mbar_arrive(&o_free[b ^ 1]);
 #pragma unroll
         for (int j = 0; j < NQT; ++j) acc[j] = fmaf(scl[j], o[j], acc[j]);
-        if (tid == 0) done_tiles = it;
       }
       pending = true;
 
       if (last) {
         // End of this CTA's part of the unit: this tile's O^T, then the unit's segment (or its output).
-        if (!mbar_wait(&bar_o[buf], buf_parity)) abort_flag = 1;
+        if (!mbar_wait(&o_full[b], par)) abort_flag = 1;
         tc_fence_after();
         __syncwarp();
         float o[NQP];
-        tmem_ld16(tbase + lane_off + 2 * NQP + buf * NQP, o);
+        tmem_ld16(tbase + lane_off + 2 * NQP + b * NQP, o);
+        tc_fence_before();
+        mbar_arrive(&o_free[b]);
 #pragma unroll
         for (int j = 0; j < NQT; ++j) acc[j] += o[j];
         pending = false;
-        if (tid == 0) done_tiles = it + 1;
-#pragma unroll
-        for (int j = 0; j < NQT; ++j) {
-          float v = lpart[j];
-#pragma unroll
-          for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
-          if (lane == 0) red[warp * NQP + j] = v;
+        {
+          int col;
+          const float v = butterfly<NQT, false>(lpart, lane, col);
+          if (butterfly_writer<NQT>(lane)) red[warp * NQP + col] = v;
         }
         named_sync(1, 128);
-        const int seg = (int)(blockIdx.x - unit_first / per);
-        const bool whole = (unit_first + w.tiles - 1) / per == unit_first / per;
+        const int seg = (int)(blockIdx.x - unit_pos0 / per);
+        const bool whole = (unit_pos0 + kTileCost * (tiles - 1)) / per == unit_pos0 / per;
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
           if (j < p.nq) {
@@ -432,19 +610,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         named_sync(1, 128);
       }
-      tc_fence_before();
     }
-    if (!ok_all) abort_flag = 1;
   }
   __syncthreads();
-  if (abort_flag && tid == 0) {
-    raise_status(p.status, kStatusTimeout);
-    tc_commit(&drain);  // every MMA thread 0 issued has completed once this arrives
-    mbar_wait(&drain, 0);
-    // Let TMA loads that were issued but not consumed land before the CTA's shared memory goes away (at most
-    // three tiles are in flight, so each slot appears once in these windows).
-    for (int i = done_tiles; i < issued_k; ++i) mbar_wait(&full[2 * (i % 3)], (i / 3) & 1);
-    for (int i = done_tiles; i < issued_v; ++i) mbar_wait(&full[2 * (i % 3) + 1], (i / 3) & 1);
+  if (abort_flag) {
+    if (tid == 0) raise_status(p.status, kStatusTimeout);
+    if (tid == 5 * 32) {
+      tc_commit(&drain);  // every MMA the issuer thread issued has completed once this arrives
+      mbar_wait(&drain, 0);
+    }
+    if (tid == 4 * 32) {
+      // Let the last load of every slot land before the CTA's shared memory goes away (a slot is refilled only
+      // after its previous load completed and was consumed).
+      for (int i = issued_k > HALF ? issued_k - HALF : 0; i < issued_k; ++i) mbar_wait(&full[i % HALF], (i / HALF) & 1);
+      for (int i = issued_v > HALF ? issued_v - HALF : 0; i < issued_v; ++i)
+        mbar_wait(&full[HALF + i % HALF], (i / HALF) & 1);
+      for (int i = q_issued > 2 ? q_issued - 2 : 0; i < q_issued; ++i) mbar_wait(&q_fill[i & 1], (i >> 1) & 1);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -452,6 +634,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }
+  OMNI_TRACE_CTA(1);
 }
 
 // Merges the segments of each (query row, head): out = sum w_s o_s / sum w_s l_s, plus (beam search) the splits
@@ -469,8 +652,9 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   long long tot = 0, pre = 0;
   for (int i = t; i < p.groups; i += 128) {
     const long long n = (unit_need(p, i) + BN - 1) / BN;
-    tot += n * p.heads;
-    if (i < g) pre += n * p.heads;
+    const long long c = unit_cost(p, n) * p.heads;
+    tot += c;
+    if (i < g) pre += c;
     if (i == g) unit_tiles = n;
   }
 #pragma unroll
@@ -485,24 +669,29 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   __syncthreads();
   const long long total = red_total[0] + red_total[1] + red_total[2] + red_total[3];
   const long long tiles = unit_tiles;
-  const long long start = red_pre[0] + red_pre[1] + red_pre[2] + red_pre[3] + (long long)h * tiles;
+  const long long pos0 =
+      red_pre[0] + red_pre[1] + red_pre[2] + red_pre[3] + (long long)h * unit_cost(p, tiles) + p.unit_cost;
   if (t == 0 && h == 0 && row % p.nq == 0) {
     const int64_t raw = p.lengths[g] + (p.causal ? p.nq - 1 : 0);
     if (p.lengths[g] < 0 || raw > p.cap) raise_status(p.status, kStatusIndex);
   }
-  const long long per = total > 0 ? (total + grid - 1) / grid : 1;
-  const int nseg = tiles > 0 ? (int)((start + tiles - 1) / per - start / per + 1) : 0;
+  const long long per = max((total + grid - 1) / grid, (long long)kTileCost);
+  const int nseg = tiles > 0 ? (int)((pos0 + kTileCost * (tiles - 1)) / per - pos0 / per + 1) : 0;
   if (nseg == 1 && extra_ml == nullptr && p.out != nullptr) return;  // finished by the pass
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the pass (and its partials) complete
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + rh * p.st;
   const float2* ml2 = extra_ml ? reinterpret_cast<const float2*>(extra_ml) + rh * extra_st : nullptr;
+  // Segments that saw no key (sum 0) take no part, whatever their max.
   float mx = -INFINITY;
-  for (int s = 0; s < nseg; ++s) mx = fmaxf(mx, ml[s].x);
-  for (int s = 0; ml2 && s < extra_st; ++s) mx = fmaxf(mx, ml2[s].x);
+  for (int s = 0; s < nseg; ++s)
+    if (ml[s].y > 0.f) mx = fmaxf(mx, ml[s].x);
+  for (int s = 0; ml2 && s < extra_st; ++s)
+    if (ml2[s].y > 0.f) mx = fmaxf(mx, ml2[s].x);
   float o = 0.f, l = 0.f;
   if (mx != -INFINITY) {
     for (int s = 0; s < nseg; ++s) {
       const float2 e = ml[s];
-      if (e.x != -INFINITY) {
+      if (e.y > 0.f) {
         const float wgt = ex2(e.x - mx);
         o = fmaf(wgt, p.part_o[(rh * p.st + s) * D + t], o);
         l = fmaf(wgt, e.y, l);
@@ -510,7 +699,7 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
     }
     for (int s = 0; ml2 && s < extra_st; ++s) {
       const float2 e = ml2[s];
-      if (e.x != -INFINITY) {
+      if (e.y > 0.f) {
         const float wgt = ex2(e.x - mx);
         o = fmaf(wgt, extra_o[(rh * extra_st + s) * D + t], o);
         l = fmaf(wgt, e.y, l);
@@ -546,6 +735,20 @@ bool make_cache_map(CUtensorMap* map, const void* base, int64_t rows, int heads,
   return r == CUDA_SUCCESS;
 }
 
+// Queries [rows, heads, 128] as 16-row boxes of one head (two 64-column boxes per unit), 128-byte swizzle.
+bool make_query_map(CUtensorMap* map, const void* q, int64_t rows, int heads) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)NQP};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace tcattn
 
 bool tc_path_enabled(int dtype, int dim, int nq) {
@@ -561,35 +764,77 @@ int tc_segments(int64_t keys) { return (int)((keys + tcattn::BN - 1) / tcattn::B
 
 int tc_grid() { return device_sm_count(); }
 
+// Tiles the producers prefetch into L2 ahead of their loads (OMNIASR_TC_PREFETCH overrides the default).
+int tc_prefetch() {
+  static const int n = [] {
+    const char* e = getenv("OMNIASR_TC_PREFETCH");
+    return e ? atoi(e) : 4;
+  }();
+  return n < 0 ? 0 : n;
+}
+
+// Cost of a unit's start and epilogue in tile-eighths (OMNIASR_TC_UNIT_COST overrides the default of one tile).
+int tc_unit_cost() {
+  static const int c = [] {
+    const char* e = getenv("OMNIASR_TC_UNIT_COST");
+    return e ? atoi(e) : 8;
+  }();
+  return c < 0 ? 0 : c;
+}
+
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream) {
   using namespace tcattn;
   CUtensorMap kmap, vmap;
+  CUtensorMap qmap;
   if (!make_cache_map(&kmap, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
-      !make_cache_map(&vmap, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos))
+      !make_cache_map(&vmap, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
+      !make_query_map(&qmap, p.q, (int64_t)p.groups * p.nq, p.heads))
     return cudaErrorInvalidValue;
   p.cap = cache_len < keys ? cache_len : keys;
   p.st = tc_segments(keys);
   p.grid = tc_grid();
-  auto kern = p.nq <= 1 ? attn_tc_kernel<1> : p.nq <= 2 ? attn_tc_kernel<2> : p.nq <= 4 ? attn_tc_kernel<4>
-            : p.nq <= 8 ? attn_tc_kernel<8> : attn_tc_kernel<16>;
-  static bool configured[5] = {false, false, false, false, false};
+  p.unit_cost = tc_unit_cost();
+  p.prefetch = tc_prefetch();
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, Params);
+  static const Kern table[5] = {attn_tc_kernel<1, 6>, attn_tc_kernel<2, 6>, attn_tc_kernel<4, 6>,
+                                attn_tc_kernel<8, 6>, attn_tc_kernel<16, 6>};
   const int ci = p.nq <= 1 ? 0 : p.nq <= 2 ? 1 : p.nq <= 4 ? 2 : p.nq <= 8 ? 3 : 4;
+  const Kern kern = table[ci];
+  const int bytes = Smem<6>::BYTES;
+  static bool configured[5] = {};
   if (!configured[ci]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
     configured[ci] = true;
   }
-  kern<<<p.grid, THREADS, SMEM_BYTES, stream>>>(kmap, vmap, p);
+  kern<<<p.grid, THREADS, bytes, stream>>>(kmap, vmap, qmap, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o, const float* extra_ml, int extra_st,
                               cudaStream_t stream) {
   using namespace tcattn;
-  combine_tc_kernel<<<(unsigned)((int64_t)p.groups * p.nq * p.heads), 128, 0, stream>>>(
-      p, p.grid, reinterpret_cast<__nv_bfloat16*>(out), extra_o, extra_ml, extra_st);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the combine's blocks start (and compute their unit's place) while the pass
+  // drains, and wait for it (griddepcontrol.wait) before reading its partials.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((int64_t)p.groups * p.nq * p.heads));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_tc_kernel, p, p.grid, o, extra_o, extra_ml, extra_st);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // no programmatic launch here: an ordinary one
+    combine_tc_kernel<<<cfg.gridDim, cfg.blockDim, 0, stream>>>(p, p.grid, o, extra_o, extra_ml, extra_st);
+    e = cudaGetLastError();
+  }
+  return e;
 }
 
 }  // namespace omni

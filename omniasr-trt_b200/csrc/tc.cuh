@@ -26,6 +26,23 @@ OMNI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int
       : "memory");
 }
 
+// 3-D tiled load into this CTA's shared memory (no multicast), completion on `bar`.
+OMNI_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Prefetches a 4-D box into L2 (no shared memory, no completion tracking).
+OMNI_DEV void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // ---- descriptors -----------------------------------------------------------------------------
 
 constexpr uint32_t kLayoutNone = 0;   // no swizzle: 8-row x 16-byte core matrices
