@@ -88,6 +88,9 @@ OMNI_DEV int64_t unit_need(const Params& p, int g) {
 //   pre(g) + h * ucost(g) + unit_cost + kTileCost * t,   pre(g) = sum over earlier groups of heads * ucost.
 // CTA b owns the tiles whose position lies in [b * per, (b + 1) * per), per = ceil(total cost / grid).
 constexpr int64_t kTileCost = 8;
+#ifndef OMNI_TC_L2_PROMOTION
+#define OMNI_TC_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B  // L2 fill granularity of the K/V boxes
+#endif
 constexpr int kSmemGroups = 256;  // groups whose lengths the pass keeps in shared memory
 
 OMNI_DEV int64_t unit_cost(const Params& p, int64_t tiles) { return tiles > 0 ? p.unit_cost + kTileCost * tiles : 0; }
@@ -730,7 +733,7 @@ bool make_cache_map(CUtensorMap* map, const void* base, int64_t rows, int heads,
   cuuint32_t box[4] = {64, (cuuint32_t)BN, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, OMNI_TC_L2_PROMOTION,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -768,7 +771,7 @@ int tc_grid() { return device_sm_count(); }
 int tc_prefetch() {
   static const int n = [] {
     const char* e = getenv("OMNIASR_TC_PREFETCH");
-    return e ? atoi(e) : 4;
+    return e ? atoi(e) : 0;  // measured: prefetching past the ring only adds DRAM traffic
   }();
   return n < 0 ? 0 : n;
 }

@@ -1,0 +1,107 @@
+"""The reference's own decoders running on these kernels (drop-in), against the reference's own PyTorch paths.
+
+The reference package (Wataru-Nakata/omniasr-trt, pure Python) is imported from ``baseline/_ref`` where it is
+installed next to this repository; ``omniasr_b200.dropin.install()`` swaps its ``omniasr_trt.kernels``. These
+restate the reference's CUDA integration tests (tests/test_kernels.py:58-95, :129-150; tests/test_spec.py:111-130)
+with the same small random model (tests/test_decode.py:17-28): token sequences must be identical to the unfused
+PyTorch step and to the reference-order loops.
+"""
+
+import sys
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+REF = ROOT / "baseline" / "_ref"
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU"),
+    pytest.mark.skipif(not (REF / "omniasr_trt" / "decode.py").exists(), reason="reference package not installed"),
+]
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    from omniasr_b200 import dropin
+    from omniasr_b200 import kernels as ours
+
+    k = dropin.install()
+    from omniasr_trt import beam, decode, llm, modeling, spec
+
+    assert decode.kernels is k and spec.kernels is k and beam.kernels is k
+    assert k.rope_kv is ours.rope_kv and k.decode_attention is ours.decode_attention
+    return {"decode": decode, "spec": spec, "beam": beam, "llm": llm, "modeling": modeling, "kernels": k}
+
+
+class FakeTokenizer:
+    def decode(self, ids):
+        return " ".join(map(str, ids))
+
+
+def small_model(modeling, seed=0, vocab=12):
+    """The reference tests' tiny random model (tests/test_decode.py:17-28), fp32 on the GPU."""
+    torch.manual_seed(seed)
+    enc = modeling.EncoderConfig(model_dim=16, num_layers=2, num_heads=2, ffn_dim=32, feature_dim=8,
+                                 conv_layers=((8, 10, 5), (8, 3, 2), (8, 2, 2)), pos_kernel=4, pos_groups=2)
+    dec = modeling.DecoderConfig(model_dim=32, num_layers=2, num_heads=2, ffn_dim=24, vocab_size=vocab, num_langs=5,
+                                 max_seq_len=8192)
+    m = modeling.LLMModel(enc, dec).double().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_(0, 0.5)
+        m.final_proj.weight.mul_(4)
+    m = m.float().cuda()
+    m.rope = modeling.rope_table(m.dec_cfg, "cuda")
+    return m
+
+
+def test_fused_greedy_decoder_matches_torch_path(ref):
+    m = small_model(ref["modeling"], seed=2)
+    torch.manual_seed(3)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (5, 33, 17, 60)]
+    dec = ref["decode"].GreedyDecoder
+    a = dec(m, max_batch=4, sync_every=8, fused=False, graphs=False, reserve=64).generate(ctxs)
+    fast = dec(m, max_batch=4, sync_every=8, fused=True, graphs=True, reserve=64)
+    assert fast.fused
+    assert fast.generate(ctxs) == a
+
+
+def test_fused_streams_across_calls(ref):
+    m = small_model(ref["modeling"], seed=7)
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer(), max_batch=3)
+    dec = ref["decode"].GreedyDecoder(m, max_batch=3, sync_every=4, fused=True, graphs=True, reserve=8)
+    torch.manual_seed(8)
+    for n, lengths in ((7, (250, 40, 5, 251, 90, 12, 248)), (2, (30, 8)), (5, (60, 252, 9, 33, 100)), (1, (17,))):
+        ctxs = [torch.randn(k, 32, device="cuda") for k in lengths[:n]]
+        assert dec.generate(ctxs) == [t.greedy_reference(c) for c in ctxs], (n, lengths)
+        torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("beams,length_norm", [(3, False), (5, True)])
+def test_fused_beam_decoder(ref, beams, length_norm):
+    m = small_model(ref["modeling"], seed=16)
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    dec = ref["beam"].BeamDecoder(m, beams=beams, length_norm=length_norm, max_batch=3, sync_every=4, fused=True,
+                                  graphs=True, reserve=8)
+    torch.manual_seed(17)
+    for lengths in ((250, 40, 5, 251, 90), (30, 8), (60, 252, 9, 33)):
+        ctxs = [torch.randn(k, 32, device="cuda") for k in lengths]
+        assert dec.generate(ctxs) == [t.beam_reference(c, beams, length_norm) for c in ctxs], lengths
+        torch.cuda.synchronize()
+
+
+def test_speculative_decoder_same_tokens_as_greedy(ref):
+    """Drafted steps (draft_attention for 1 + 4 queries per row) give the greedy search's tokens."""
+    m = small_model(ref["modeling"], seed=21)
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    torch.manual_seed(22)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (40, 7, 251, 90, 13, 60)]
+    want = [t.greedy_reference(c) for c in ctxs]
+    dec = ref["spec"].SpecDecoder(m, draft_tokens=4, max_batch=4, sync_every=3, reserve=8)
+    dec.drafts = lambda j: (want[j] + [5, 6, 7], 0)  # perfect drafts: several tokens per step
+    assert dec.generate(ctxs) == want
+    assert dec.stats["tokens"] / dec.stats["rows_steps"] > 1.5
