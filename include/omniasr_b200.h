@@ -117,6 +117,23 @@ int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_
                            int64_t dst_row_stride, const void* parent, int parent_is_int64, int rows,
                            int64_t row_bytes, int* status, cudaStream_t stream);
 
+/* Flash-decode for callers that cannot allocate device memory (no counterpart in the reference, whose
+ * wrappers allocate their partials with torch.empty): the same computation and arguments as
+ * omniasr_decode_attention() minus the workspace, which here is a device array inside this library of
+ * omniasr_noalloc_scratch_bytes() bytes (8 MiB), held on every GPU that loads the library until the process
+ * exits. For a host whose device memory is owned by another allocator, or a plugin interface that hands over
+ * only the input and output buffers. Shapes whose split partials exceed the array are rejected with
+ * OMNIASR_ERR_WORKSPACE. The first call on a device looks up the array's address (cudaGetSymbolAddress) and
+ * should come before any stream capture. All calls on a device share the array: calls whose kernels overlap on
+ * the GPU race, so order them (same stream, or events). */
+int omniasr_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                                     int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                                     const int64_t* lengths, void* out, int batch, int heads, int dim, int keys,
+                                     float scale, int dtype, int* status, cudaStream_t stream);
+
+/* Size in bytes of the device scratch array behind omniasr_decode_attention_noalloc(). */
+size_t omniasr_noalloc_scratch_bytes(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,11 @@ int check_cache(const char* name, const void* k, const void* v, int64_t rows, in
 
 }  // namespace
 
+namespace omni {
+// Sets this thread's last-error message (for entry points defined in other files); returns `code`.
+int set_last_error(int code, const char* message) { return fail(code, "%s", message); }
+}  // namespace omni
+
 extern "C" {
 
 int omniasr_abi_version(void) { return 1; }
