@@ -109,6 +109,18 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
                            void* out, int groups, int beams, int heads, int dim, int ctx_keys, float scale, int dtype,
                            void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
 
+/* Causal prefill attention (bf16, head_dim 128): out[b, h, w] = softmax(q[b, h, w] . k[b, h, :w+1]^T * scale)
+ * . v[b, h, :w+1] for every position w < width. q, k, v and out are [batch, heads, width, 128] given by base
+ * pointer and (row, head, position) element strides (k and v are typically views of the KV cache; out may be a
+ * [batch, width, heads, 128] buffer seen through its strides). Replaces the reference's prefill
+ * F.scaled_dot_product_attention(q, k, v, is_causal=True), omniasr_trt/decode.py:171. */
+int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_stride_head, int64_t q_stride_pos,
+                              const void* k, int64_t k_stride_row, int64_t k_stride_head, int64_t k_stride_pos,
+                              const void* v, int64_t v_stride_row, int64_t v_stride_head, int64_t v_stride_pos,
+                              void* out, int64_t out_stride_row, int64_t out_stride_head, int64_t out_stride_pos,
+                              int batch, int heads, int width, int dim, float scale, int dtype, int* status,
+                              cudaStream_t stream);
+
 /* Beam reorder: dst row r (r < rows) = src row parent[r], byte-exact; rows are row_bytes long,
  * strides in bytes; parent is int32 (parent_is_int64 = 0) or int64. src and dst must not overlap.
  * Replaces the K/V `index_select(0, parent)` of omniasr_trt/llm.py:237-238 and the pointer /

@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "gather.cuh"
 #include "omniasr_b200.h"
+#include "prefill.cuh"
 #include "rope_kv.cuh"
 
 namespace {
@@ -377,6 +378,51 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
   if (int e = cuda_status(omni::launch_split(dtype, dim, true, pg, b, (int)rows, stream), "generated split launch"))
     return e;
   return cuda_status(omni::launch_combine(dtype, dim, po, pml, out, rows * heads, st, stream), "combine launch");
+}
+
+int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_stride_head, int64_t q_stride_pos,
+                              const void* k, int64_t k_stride_row, int64_t k_stride_head, int64_t k_stride_pos,
+                              const void* v, int64_t v_stride_row, int64_t v_stride_head, int64_t v_stride_pos,
+                              void* out, int64_t out_stride_row, int64_t out_stride_head, int64_t out_stride_pos,
+                              int batch, int heads, int width, int dim, float scale, int dtype, int* status,
+                              cudaStream_t stream) {
+  const char* name = "prefill_attention";
+  if (dtype != OMNIASR_BF16 || dim != 128)
+    return fail(OMNIASR_ERR_UNSUPPORTED, "%s: bf16 with head_dim 128 only (dtype %d, head_dim %d)", name, dtype, dim);
+  if (int e = check_device()) return e;
+  if (batch < 0 || heads <= 0 || width < 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: shape", name);
+  if (batch == 0 || width == 0) return ok();
+  if (!q || !k || !v || !out) return fail(OMNIASR_ERR_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: pointers must be 16-byte aligned", name);
+  const int64_t strides[12] = {q_stride_row, q_stride_head, q_stride_pos, k_stride_row, k_stride_head, k_stride_pos,
+                               v_stride_row, v_stride_head, v_stride_pos, out_stride_row, out_stride_head,
+                               out_stride_pos};
+  for (int64_t st : strides)
+    if (!stride_ok(st, dtype)) return fail(OMNIASR_ERR_ARGUMENT, "%s: strides must keep 16-byte alignment", name);
+  omni::PrefillArgs a;
+  a.q = q;
+  a.q_sb = q_stride_row;
+  a.q_sh = q_stride_head;
+  a.q_sw = q_stride_pos;
+  a.k = k;
+  a.k_sb = k_stride_row;
+  a.k_sh = k_stride_head;
+  a.k_sw = k_stride_pos;
+  a.v = v;
+  a.v_sb = v_stride_row;
+  a.v_sh = v_stride_head;
+  a.v_sw = v_stride_pos;
+  a.out = out;
+  a.o_sb = out_stride_row;
+  a.o_sh = out_stride_head;
+  a.o_sw = out_stride_pos;
+  a.batch = batch;
+  a.heads = heads;
+  a.width = width;
+  a.scale = scale;
+  a.status = status;
+  return cuda_status(omni::launch_prefill(a, stream), "prefill launch");
 }
 
 int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_rows, void* dst,

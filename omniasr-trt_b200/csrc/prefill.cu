@@ -1,0 +1,440 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), bf16, head_dim 128.
+//
+// out[b, w, h] = softmax(q[b, h, w] . k[b, h, :w+1]^T * scale) . v[b, h, :w+1]   for w < W
+// (F.scaled_dot_product_attention(q, k, v, is_causal=True) of the reference's prefill, decode.py:171; the
+// reference-semantics form is modeling.py:398-399). Right-padded rows need nothing special: a valid query never
+// sees a later (pad) key.
+//
+// Work unit: (row b, head h, 128-query tile qt) over key tiles 0..qt; units are taken heaviest first by a
+// persistent grid of one CTA per SM. Roles (224 threads):
+//   warp 4  TMA: the query tile (two 64-column boxes, 128-byte swizzle) and the K tiles (3-slot ring)
+//   warp 6  TMA: the V tiles (2-slot ring)
+//   warp 5  MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered), then O += P V with P read
+//           from TMEM (the tcgen05 "A in TMEM" form) and V as an MN-major operand; O accumulates in TMEM
+//   warps 0-3 softmax, thread t = query row t of the tile: the row max and sum are thread-local; the running
+//           max is raised only when a row's scores pass it by 2^8, and only then is the row's O rescaled in TMEM
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512) (P: bf16 pairs, 64 columns).
+
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "attention.cuh"
+#include "prefill.cuh"
+#include "tc.cuh"
+
+namespace omni {
+namespace prefill {
+
+constexpr int D = 128;
+constexpr int BM = 128;  // queries per tile
+constexpr int BN = 128;  // keys per tile
+constexpr int TILE = BN * D * 2;
+constexpr int BOX = BN * 64 * 2;
+constexpr int KS = 3, VS = 2;
+constexpr int Q_OFF = 0;
+constexpr int K_OFF = Q_OFF + TILE;
+constexpr int V_OFF = K_OFF + KS * TILE;
+constexpr int SMEM_BYTES = V_OFF + VS * TILE + 1024;
+constexpr int THREADS = 224;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, 0, 0);
+constexpr uint32_t IDESC_O = idesc_bf16(BM, D, 0, 1);
+constexpr float kRescale = 8.f;
+
+struct Params {
+  int batch, heads, width, qtiles;
+  float qscale;  // scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t out_sb, out_sw, out_sh;  // out[b, w, h, :] strides (elements)
+  int* status;
+};
+
+// D (TMEM) = A (TMEM) x B (smem) [+ D]; issued by one thread.
+OMNI_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+OMNI_DEV void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+OMNI_DEV void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+OMNI_DEV void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+OMNI_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Unit u (heaviest query tiles first) -> (b, h, qt).
+OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
+  const int bh_count = p.batch * p.heads;
+  qt = p.qtiles - 1 - u / bh_count;
+  const int bh = u % bh_count;
+  b = bh / p.heads;
+  h = bh % p.heads;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
+  __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_ready, o_free, drain;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  __shared__ volatile int issued_k, issued_v, issued_q;  // loads the producers issued
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int units = p.batch * p.heads * p.qtiles;
+  if ((int)blockIdx.x >= units) return;
+
+  if (tid == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&pv_done[s], 1);
+      mbar_init(&s_free[s], 128);
+      mbar_init(&p_full[s], 128);
+    }
+    mbar_init(&o_ready, 1);
+    mbar_init(&o_free, 128);
+    mbar_init(&drain, 1);
+    mbar_fence_init();
+    abort_flag = 0;
+    issued_k = issued_v = issued_q = 0;
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  unsigned char* qs = smem + Q_OFF;
+
+  if (warp == 4 || warp == 6) {
+    // ------------------------------------------------------------------ producers
+    if (lane == 0) {
+      const bool is_k = warp == 4;
+      prefetch_tmap(is_k ? &kmap : &vmap);
+      if (is_k) prefetch_tmap(&qmap);
+      int tile = 0, nunit = 0;
+      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
+        int b, h, qt;
+        unit_of(p, u, b, h, qt);
+        if (is_k) {
+          if (nunit >= 1 && !mbar_wait(&q_empty, (nunit - 1) & 1)) {
+            abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full, TILE);
+          tma_load_4d(qs, &qmap, 0, qt * BM, h, b, &q_full);
+          tma_load_4d(qs + BOX, &qmap, 64, qt * BM, h, b, &q_full);
+          issued_q = nunit + 1;
+        }
+        for (int kt = 0; kt <= qt && !abort_flag; ++kt, ++tile) {
+          const int ns = is_k ? KS : VS;
+          const int slot = tile % ns, use = tile / ns;
+          uint64_t* empty = is_k ? &k_empty[slot] : &v_empty[slot];
+          uint64_t* full = is_k ? &k_full[slot] : &v_full[slot];
+          if (use >= 1 && !mbar_wait(empty, (use - 1) & 1)) {
+            abort_flag = 1;
+            break;
+          }
+          unsigned char* dst = smem + (is_k ? K_OFF : V_OFF) + slot * TILE;
+          mbar_arrive_expect_tx(full, TILE);
+          tma_load_4d(dst, is_k ? &kmap : &vmap, 0, kt * BN, h, b, full);
+          tma_load_4d(dst + BOX, is_k ? &kmap : &vmap, 64, kt * BN, h, b, full);
+          if (is_k) issued_k = tile + 1;
+          else issued_v = tile + 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int tile = 0, nunit = 0;
+      bool ok = true;
+      auto scores = [&](int t, int kt_local) -> bool {  // S[t & 1] = Q K(t)^T
+        const int sb = t & 1, su = t >> 1;
+        const int slot = t % KS;
+        if (su >= 1 && !mbar_wait(&s_free[sb], (su - 1) & 1)) return false;
+        if (!mbar_wait(&k_full[slot], (t / KS) & 1)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_addr(qs), ka = smem_addr(smem + K_OFF + slot * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = smem_desc(qa + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
+          const uint64_t bd = smem_desc(ka + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
+          mma_bf16_ss(tbase + COL_S + sb * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[sb]);
+        tc_commit(&k_empty[slot]);
+        (void)kt_local;
+        return true;
+      };
+      auto values = [&](int t, bool first_of_unit) -> bool {  // O += P[t & 1] V(t)
+        const int pb = t & 1, pu = t >> 1;
+        const int slot = t % VS;
+        if (first_of_unit && nunit >= 1 && !mbar_wait(&o_free, (nunit - 1) & 1)) return false;
+        if (!mbar_wait(&p_full[pb], pu & 1)) return false;
+        if (!mbar_wait(&v_full[slot], (t / VS) & 1)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_addr(smem + V_OFF + slot * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = smem_desc(va + kk * 2048, BOX, 1024, kLayoutSw128);
+          mma_bf16_ts(tbase + COL_O, tbase + COL_P + pb * 64 + kk * 8, bd, IDESC_O,
+                      (first_of_unit && kk == 0) ? 0u : 1u);
+        }
+        tc_commit(&pv_done[pb]);
+        tc_commit(&v_empty[slot]);
+        return true;
+      };
+      for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
+        int b, h, qt;
+        unit_of(p, u, b, h, qt);
+        if (!mbar_wait(&q_full, nunit & 1)) {
+          ok = false;
+          break;
+        }
+        const int t0 = tile;
+        for (int kt = 0; kt <= qt && ok; ++kt, ++tile) {
+          ok = scores(tile, kt);
+          if (ok && kt == qt) tc_commit(&q_empty);  // the unit's last use of Q
+          if (ok && kt > 0) ok = values(tile - 1, tile - 1 == t0);
+        }
+        if (ok) ok = values(tile - 1, tile - 1 == t0);
+        if (ok) tc_commit(&o_ready);
+      }
+      if (!ok) abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax (thread = query row)
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    int tile = 0, nunit = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++nunit) {
+      int b, h, qt;
+      unit_of(p, u, b, h, qt);
+      float m = -INFINITY, l = 0.f;
+      for (int kt = 0; kt <= qt; ++kt, ++tile) {
+        const int sb = tile & 1;
+        const uint32_t spar = (tile >> 1) & 1;
+        const bool diag = kt == qt;
+        if (!mbar_wait(&s_full[sb], spar)) abort_flag = 1;
+        tc_fence_after();
+        __syncwarp();
+        const uint32_t scol = tbase + lane_off + COL_S + sb * 128;
+        // Pass 1: the row's max over this tile (keys past the query masked on the diagonal tile).
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(scol + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (!diag || c * 32 + i <= tid) tmax = fmaxf(tmax, v[i]);
+        }
+        tmax *= p.qscale;
+        // Raise the running max only when needed; then the row's O (built from earlier tiles) is rescaled.
+        float mnew = m;
+        if (tmax > m + kRescale) mnew = tmax;
+        const bool rescale = mnew != m && kt > 0;
+        if (__any_sync(0xffffffffu, rescale)) {
+          if (!mbar_wait(&pv_done[(tile - 1) & 1], ((tile - 1) >> 1) & 1)) abort_flag = 1;
+          tc_fence_after();
+          __syncwarp();
+          const float sc = rescale ? ex2(m - mnew) : 1.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            uint32_t w[32];
+            tmem_ld32(tbase + lane_off + COL_O + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i] * sc);
+            tmem_st32(tbase + lane_off + COL_O + c * 32, w);
+          }
+          tmem_wait_st();
+          l *= sc;
+        }
+        m = mnew;
+        // P[sb] is free once O += P V of two tiles ago has completed.
+        if (tile >= 2) {
+          if (!mbar_wait(&pv_done[sb], ((tile - 2) >> 1) & 1)) abort_flag = 1;
+          tc_fence_after();
+          __syncwarp();
+        }
+        // Pass 2: probabilities (bf16 pairs) into P[sb] and the row sum.
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(scol + c * 32, v);
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = c * 32 + 2 * i;
+            const float p0 = (!diag || k0 <= tid) ? ex2(fmaf(v[2 * i], p.qscale, -m)) : 0.f;
+            const float p1 = (!diag || k0 + 1 <= tid) ? ex2(fmaf(v[2 * i + 1], p.qscale, -m)) : 0.f;
+            l += p0 + p1;
+            w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
+                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16);
+          }
+          tmem_st16(tbase + lane_off + COL_P + sb * 64 + c * 16, w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s_free[sb]);
+        mbar_arrive(&p_full[sb]);
+      }
+      // Epilogue: O / l -> out[b, q, h, :] for the tile's valid queries.
+      if (!mbar_wait(&o_ready, nunit & 1)) abort_flag = 1;
+      tc_fence_after();
+      __syncwarp();
+      const int q = qt * BM + tid;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + (int64_t)b * p.out_sb + (int64_t)q * p.out_sw + (int64_t)h * p.out_sh;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tbase + lane_off + COL_O + c * 32, v);
+        if (q < p.width) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              w[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[8 * i + 2 * j] * inv)) |
+                     ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[8 * i + 2 * j + 1] * inv)) << 16);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free);
+      if (abort_flag) break;
+    }
+  }
+  __syncthreads();
+  if (abort_flag) {
+    if (tid == 0) raise_status(p.status, kStatusTimeout);
+    if (tid == 5 * 32) {
+      tc_commit(&drain);
+      mbar_wait(&drain, 0);
+    }
+  }
+  __syncthreads();
+  if (abort_flag && tid == 4 * 32) {
+    // Let the latest load of every slot land (a slot is refilled only after its previous load was consumed).
+    for (int i = issued_k > KS ? issued_k - KS : 0; i < issued_k; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1);
+    for (int i = issued_v > VS ? issued_v - VS : 0; i < issued_v; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1);
+    if (issued_q > 0) mbar_wait(&q_full, (issued_q - 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t w, int64_t sb, int64_t sh,
+              int64_t sw) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)b};
+  cuuint64_t strides[3] = {(cuuint64_t)sw * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace prefill
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
+  using namespace prefill;
+  CUtensorMap qm, km, vm;
+  if (!make_map(&qm, a.q, a.batch, a.heads, a.width, a.q_sb, a.q_sh, a.q_sw) ||
+      !make_map(&km, a.k, a.batch, a.heads, a.width, a.k_sb, a.k_sh, a.k_sw) ||
+      !make_map(&vm, a.v, a.batch, a.heads, a.width, a.v_sb, a.v_sh, a.v_sw))
+    return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  Params p;
+  p.batch = a.batch;
+  p.heads = a.heads;
+  p.width = a.width;
+  p.qtiles = (a.width + BM - 1) / BM;
+  p.qscale = a.scale * kLog2e;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.out_sb = a.o_sb;
+  p.out_sw = a.o_sw;
+  p.out_sh = a.o_sh;
+  p.status = a.status;
+  const int units = a.batch * a.heads * p.qtiles;
+  int grid = device_sm_count();
+  if (grid > units) grid = units;
+  if (grid <= 0) return cudaSuccess;
+  prefill_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(qm, km, vm, p);
+  return cudaGetLastError();
+}
+
+}  // namespace omni

@@ -37,6 +37,8 @@ SIGNATURES = {
                                      _p, _sz, _p, _p]),
     "omniasr_beam_attention": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _p, _i64, _p, _p, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
+    "omniasr_prefill_attention": (_i, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64,
+                                       _i64, _i64, _i, _i, _i, _i, _f, _i, _p, _p]),
     "omniasr_reorder_gather": (_i, [_p, _i64, _i64, _p, _i64, _p, _i, _i, _i64, _p, _p]),
     "omniasr_decode_attention_noalloc": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _i, _i, _f,
                                               _i, _p, _p]),

@@ -10,6 +10,8 @@ CUDA-graph capture run on these kernels unchanged:
 * :func:`draft_attention` -- a row's 1 + k draft queries, causal within them (``kernels.py:338-358``);
 * :func:`beam_attention` -- beams over their input's shared context plus their own generated keys through
   the pointer history (``kernels.py:309-332``);
+* :func:`prefill_attention` -- causal attention of prefilled contexts, the prefill's
+  ``F.scaled_dot_product_attention(is_causal=True)`` (``decode.py:171``);
 * :func:`reorder_gather` -- the beam reorder ``dst[r] = src[parent[r]]``, byte-exact (``llm.py:237-238``,
   ``beam.py:175-176``).
 
@@ -54,7 +56,8 @@ def status_word(device: torch.device | int | None = None) -> torch.Tensor:
                          (device if isinstance(device, int) else torch.device(device).index or 0)).index
     word = _status.get(index)
     if word is None:
-        word = _status[index] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        with torch.inference_mode(False):  # a normal tensor, so it can be cleared inside or outside inference mode
+            word = _status[index] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
     return word
 
 
@@ -209,6 +212,34 @@ def beam_attention(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, ctx_len:
               _ptr(gen_len), _ptr(out), groups, int(beams), heads, dim, int(ctx_keys), float(scale), dtype, _ptr(ws),
               ws.numel(), _ptr(status_word(q.device)), _stream(q.device))
     return out
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+    """Causal attention of prefilled contexts: ``q``/``k``/``v`` [B, H, W, D] (any strides, unit stride in D; k and
+    v typically cache views); query w sees keys [0, w]. Returns [B, H, W, D] in q's dtype -- a view of a
+    [B, W, H, D] buffer, so the caller's ``o.transpose(1, 2).reshape(B * W, -1)`` costs nothing. This is the
+    reference's ``F.scaled_dot_product_attention(q, k, v, is_causal=True)`` (decode.py:171): bf16 head_dim 128 runs
+    on the tensor cores; other dtypes / head dims run as a drafted verify with W queries per row."""
+    b, heads, width, dim = q.shape
+    scale = dim**-0.5 if scale is None else float(scale)
+    out = torch.empty(b, width, heads, dim, dtype=q.dtype, device=q.device)
+    if b == 0 or width == 0:
+        return out.transpose(1, 2)
+    if k.shape != q.shape or v.shape != q.shape or q.stride(3) != 1 or k.stride(3) != 1 or v.stride(3) != 1:
+        raise ValueError("prefill_attention: q, k, v must be [B, H, W, D] with unit stride in D")
+    if q.dtype == torch.bfloat16 and dim == 128:
+        _lib.call("omniasr_prefill_attention", _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k), k.stride(0),
+                  k.stride(1), k.stride(2), _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(out), out.stride(0),
+                  out.stride(2), out.stride(1), b, heads, width, dim, scale, _lib.BF16,
+                  _ptr(status_word(q.device)), _stream(q.device))
+        return out.transpose(1, 2)
+    # Every row's W queries as one draft of W tokens over its own keys: query w sees 1 + w keys.
+    if k.stride() != v.stride():  # the draft pass reads k and v through one set of strides
+        k, v = k.contiguous(), v.contiguous()
+    qq = q.transpose(1, 2).reshape(b * width, heads, dim)
+    ones = torch.ones(b, dtype=torch.int64, device=q.device)
+    o = draft_attention(qq, k, v, ones, width, width, scale)
+    return o.view(b, width, heads, dim).transpose(1, 2)
 
 
 def reorder_gather(src: torch.Tensor, parent: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

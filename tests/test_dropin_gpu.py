@@ -34,6 +34,7 @@ def ref():
 
     assert decode.kernels is k and spec.kernels is k and beam.kernels is k
     assert k.rope_kv is ours.rope_kv and k.decode_attention is ours.decode_attention
+    assert isinstance(decode.F, dropin._Functional)  # the prefill's causal SDPA runs prefill_attention
     return {"decode": decode, "spec": spec, "beam": beam, "llm": llm, "modeling": modeling, "kernels": k}
 
 
@@ -60,6 +61,8 @@ def small_model(modeling, seed=0, vocab=12):
 
 
 def test_fused_greedy_decoder_matches_torch_path(ref):
+    """Fused step (rope_kv + decode_attention, CUDA graphs) against the unfused PyTorch step; both prefill through
+    prefill_attention, which the reference-order loops of the other tests pin against PyTorch."""
     m = small_model(ref["modeling"], seed=2)
     torch.manual_seed(3)
     ctxs = [torch.randn(n, 32, device="cuda") for n in (5, 33, 17, 60)]

@@ -417,3 +417,47 @@ def test_tc_attention_uninitialised_cache_tail_is_ignored(K):
     assert not torch.isnan(out).any()
     kz, vz = kc.nan_to_num(0.0), vc.nan_to_num(0.0)
     check_attention(out, oatt.decode_attention(q, kz, vz, lengths, d**-0.5), torch.bfloat16, what="nan tail")
+
+
+# ------------------------------------------------------------------------------------------------------ prefill
+
+
+def _prefill_inputs(b, h, w, d, dtype, seed):
+    """q as the decoder makes it (rope_kv's [B*W, H, D] seen as [B, H, W, D]), k / v as cache views [B, H, W, D]."""
+    q = randn((b * w, h, d), dtype, seed).cuda().view(b, w, h, d).transpose(1, 2)
+    cap = w + 37
+    kc = randn((b + 1, h, cap, d), dtype, seed + 1).cuda()
+    vc = randn((b + 1, h, cap, d), dtype, seed + 2).cuda()
+    return q, kc[:b, :, :w], vc[:b, :, :w]
+
+
+@pytest.mark.parametrize("b,h,w", [(1, 2, 1), (2, 2, 100), (3, 2, 128), (2, 3, 129), (1, 4, 257), (2, 2, 640)])
+def test_prefill_attention_matches_oracle(K, b, h, w):
+    """bf16 head_dim 128 on the tensor cores: every query-tile / key-tile edge (1, 128, 129, 257), strided cache
+    views, the decoder's transposed q; output [B, H, W, D] (a view of [B, W, H, D])."""
+    d = 128
+    q, k, v = _prefill_inputs(b, h, w, d, torch.bfloat16, 200 + w)
+    out = K.prefill_attention(q, k, v)
+    assert out.shape == (b, h, w, d) and out.transpose(1, 2).is_contiguous()
+    want = oatt.prefill_attention(q.cpu(), k.cpu(), v.cpu())
+    check_attention(out, want, torch.bfloat16, what=f"prefill b={b} h={h} w={w}")
+    assert K.read_status() == 0
+
+
+@pytest.mark.parametrize("dtype,d,w", [(torch.float32, 16, 60), (torch.float32, 128, 130), (torch.bfloat16, 64, 90)])
+def test_prefill_attention_other_dtypes(K, dtype, d, w):
+    """fp32 (the reference's fp32 tests) and other head dims run as a W-query draft on the CUDA cores."""
+    q, k, v = _prefill_inputs(2, 2, w, d, dtype, 250 + w)
+    out = K.prefill_attention(q, k, v)
+    want = oatt.prefill_attention(q.cpu(), k.cpu(), v.cpu())
+    check_attention(out, want, dtype, 1e-4, f"prefill {dtype} d={d}")
+
+
+def test_prefill_attention_config4_shape(K):
+    """BASELINE config 4's prefill: 8 contexts x 1500 positions, 32 x 128 heads (checked on 3 of the heads)."""
+    b, h, w, d = 8, 32, 1500, 128
+    q, k, v = _prefill_inputs(b, h, w, d, torch.bfloat16, 7)
+    out = K.prefill_attention(q, k, v)
+    for hh in (0, 17, 31):
+        want = oatt.prefill_attention(q[:, hh:hh + 1].cpu(), k[:, hh:hh + 1].cpu(), v[:, hh:hh + 1].cpu())
+        check_attention(out[:, hh:hh + 1], want, torch.bfloat16, what=f"config 4 head {hh}")
