@@ -1,18 +1,25 @@
 #!/usr/bin/env python
-"""Benchmark of the omniASR-LLM decoder-attention hot path on B200 (BASELINE.json config 2).
+"""Benchmark of the omniASR-LLM decoder-attention hot path on B200.
 
-One step is the attention part of one speculative (spec-4) decoder step over a batch of 8 rows, for all 12 decoder
-layers: per layer the fused RoPE + KV-cache append of the 40 new tokens (``kernels.rope_kv``) and the verify attention
-of their 5 queries per row over the cache (``kernels.draft_attention``), 32 heads x 128, bf16, cache capacity 4096,
-cached lengths U[200, 2000] (seed 0). Every layer has its own cache, so a step reads 12 x ~145 MB of K/V, far more
-than the 126 MB L2; no flush is needed between steps.
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--workload NAME] [--layers L]
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+The default workload (``verify``) is the headline: one step is the attention part of one
+speculative (spec-4) decoder step over a batch of 8 rows, for all 12 decoder layers -- per layer the fused RoPE +
+KV-cache append of the 40 new tokens (``kernels.rope_kv``) and the verify attention of their 5 queries per row over
+the cache (``kernels.draft_attention``), 32 heads x 128, bf16, cache capacity 4096, cached lengths U[200, 2000]
+(seed 0). Every layer has its own cache, so a step reads 12 x ~145 MB of K/V, far more than the 126 MB L2; no flush
+is needed between steps. The other BASELINE configs are their own workloads, each printing one line of the same form:
 
-Under torchrun (N > 1) every rank runs its own batch of 8 rows (request-sharded data parallel, weak scaling, no
-collective on the path); the timed region is bracketed by a barrier and a device synchronisation, and the slowest
-rank's time is reported. ``--impl reference`` times the CPU port of the reference's algorithm (the oracle) on the
-host cores, rank 0 only.
+    decode   config 1: q_len-1 decode attention, batch 8, 1024 keys per row, 12 layers
+    beam     config 3: beam attention, 8 inputs x 5 beams, context U[300, 1800] shared per input, 12 layers
+    gather   config 3: the K/V-cache reorder of the beam step by int32 parents (bit-exact row gather)
+    prefill  config 4: causal prefill attention, 8 rows x 1500 frames, 12 layers (tensor-bound: TFLOP/s)
+    sweep    config 5: 64 rows sharded over the ranks, q_len 1 and 5, lengths 512 / 2048 / 8192
+
+Under torchrun (N > 1) every rank runs its own shard (request-sharded data parallel, no collective on the path);
+the timed region is bracketed by a barrier and a device synchronisation, and the slowest rank's time is reported.
+``--impl reference`` times the CPU port of the reference's algorithm (the oracle) on the host cores, rank 0 only.
+``--layers`` shrinks a workload (for profiling captures); the line then says so in ``config``.
 """
 
 from __future__ import annotations
@@ -34,100 +41,505 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-B, T, H, D, CAP, LAYERS = 8, 5, 32, 128, 4096, 12
-METRIC = "decode-attn HBM GB/s (spec-4 verify + fused RoPE/KV append, batch 8, 12 layers)"
+H, D, LAYERS = 32, 128, 12
 NOMINAL_HBM_GBS = 8000.0
+KV_TOKEN = 2 * H * D * 2  # K + V bytes of one token in one layer (bf16)
 
 
-def peaks() -> tuple[float, str]:
+def peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
-        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        d = json.loads(path.read_text())
+        return {"hbm": float(d["hbm_gbs"]), "tensor": float(d["bf16_tflops"]), "kind": "measured"}
+    return {"hbm": 6650.0, "tensor": 1590.0, "kind": "fallback"}
 
 
-def workload_lengths() -> torch.Tensor:
-    """Cached keys per row before the step, U[200, 2000] from the seed-0 CPU generator (drawn first)."""
-    return torch.randint(200, 2001, (B,), generator=torch.Generator().manual_seed(0))
+def traffic_per_launch(key: str) -> float | None:
+    """DRAM bytes per launch of a workload's dominant kernel from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / "roofline_traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith(f"{key}="):
+            return float(line.split("=", 1)[1])
+    return None
 
 
-def keys_bucket(lengths: torch.Tensor) -> int:
-    """The decoders' key bucket: the last query's keys rounded up to 256 (decode.py:349)."""
-    return int((int(lengths.max()) + T + 255) // 256 * 256)
+def cpu_gen(seed: int = 0) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
 
 
-def algorithmic_bytes(lengths: torch.Tensor) -> dict:
-    """Unique HBM bytes one layer must move (bf16): K/V of every key the last query of a row sees, the new qkv rows,
-    their cos/sin rows, the appended K/V, the rotated q (written, then read) and the output."""
-    kv_read = int((16384 * (lengths + T)).sum())  # 2 (K, V) x H x D x 2 B per key
-    qkv = B * T * 3 * H * D * 2
-    cs = B * T * (D // 2) * 2 * 4
-    append = B * T * 2 * H * D * 2
-    q_rw = 2 * B * T * H * D * 2
-    out = B * T * H * D * 2
-    attention = kv_read + B * T * H * D * 2 + out  # what draft_attention itself must move
-    return {"layer": kv_read + qkv + cs + append + q_rw + out, "attention": attention, "kv_read": kv_read}
+def rope_table(positions: int, theta: float = 10_000.0) -> torch.Tensor:
+    """The decoder's cos/sin input table [positions, D/2, 2] float32 (the reference's modeling.py:293-298)."""
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    angles = torch.outer(torch.arange(positions, dtype=torch.float32), inv)
+    return torch.stack([torch.cos(angles), torch.sin(angles)], -1)
 
 
-# --------------------------------------------------------------------------------------------------------- GPU arm
+def keys_bucket(n: int) -> int:
+    """The decoders' key bucket: rounded up to 256 (decode.py:349)."""
+    return (n + 255) // 256 * 256
 
 
-class Step:
-    """The 12-layer attention step, captured once as a CUDA graph through the public API."""
+# ------------------------------------------------------------------------------------------------------ workloads
 
-    def __init__(self, device: torch.device, seed: int):
+
+class Workload:
+    """One step of a BASELINE config through the public API (``omniasr_b200.kernels``), captured as a CUDA graph.
+
+    ``run(ev)`` issues the step's launches; with ``ev`` it records a pair of events around every launch of the
+    dominant (roofline) call. ``step_units`` is the algorithmic bytes (or FLOPs) of one step on this rank and
+    ``roof_units`` those of one roofline call."""
+
+    name = ""
+    metric = ""
+    unit = "GB/s"
+    bound = "hbm"
+    roof_kernel = ""
+    traffic_key = ""
+    calls_per_layer = 1
+
+    def __init__(self, device: torch.device, rank: int, world: int, layers: int):
         from omniasr_b200 import kernels
-        from oracle.rope import rope_table
 
         self.K = kernels
         assert kernels.available(device), "needs a B200 (compute capability 10.0) and the built library"
-        self.device = device
-        lengths = workload_lengths()
-        self.lengths_cpu = lengths
-        self.keys = keys_bucket(lengths)
-        gen = torch.Generator(device=device).manual_seed(seed)
-        self.kc = [torch.randn(B, H, CAP, D, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(LAYERS)]
-        self.vc = [torch.randn(B, H, CAP, D, generator=gen, device=device, dtype=torch.bfloat16) for _ in range(LAYERS)]
-        self.qkv = torch.randn(LAYERS, B * T, 3 * H * D, generator=gen, device=device, dtype=torch.bfloat16)
-        self.cs = rope_table(D, CAP).to(device)
-        j = torch.arange(T)
-        self.pos = (lengths[:, None] + j).reshape(-1).to(device)  # input positions of the 5 fed tokens
-        self.slots = torch.arange(B).repeat_interleave(T).to(device)
-        self.att_len = (lengths + 1).to(device)  # query i of a row sees lengths + 1 + i keys (spec.py:95)
-        self.scale = D**-0.5
-        self.graph = None
-        self.outs = None
-        self.ev = None
+        self.device, self.rank, self.world, self.layers = device, rank, world, layers
+        self.gen = torch.Generator(device=device).manual_seed(1000 + rank)
+        self.h2d: list[torch.Tensor] = []  # inputs refreshed from pinned host memory every end-to-end step
+        self.d2h: list[torch.Tensor] = []  # results read back every end-to-end step
 
-    def run(self, timed_events: bool = False):
+    def randn(self, *shape):
+        return torch.randn(*shape, generator=self.gen, device=self.device, dtype=torch.bfloat16)
+
+    def run(self, ev=None):
+        raise NotImplementedError
+
+    def config(self) -> dict:
+        raise NotImplementedError
+
+    def launches_per_step(self) -> int:
+        return self.calls_per_layer * self.layers
+
+
+class Verify(Workload):
+    """fused RoPE/KV append + spec-4 verify attention, batch 8, 12 layers."""
+
+    name = "verify"
+    metric = "decode-attn HBM GB/s (spec-4 verify + fused RoPE/KV append, batch 8, 12 layers)"
+    roof_kernel = "draft_attention (split + combine launches of one layer)"
+    traffic_key = "draft_attention_config2_bytes_per_call"
+    B, T, CAP = 8, 5, 4096
+    calls_per_layer = 3  # rope_kv, attention pass, combine
+
+    @classmethod
+    def lengths(cls) -> torch.Tensor:
+        """Cached keys per row before the step, U[200, 2000] from the seed-0 CPU generator (drawn first)."""
+        return torch.randint(200, 2001, (cls.B,), generator=cpu_gen(0))
+
+    @classmethod
+    def bytes(cls, lengths: torch.Tensor) -> dict:
+        """Unique HBM bytes one layer must move (bf16): K/V of every key the last query of a row sees, the new qkv
+        rows, their cos/sin rows, the appended K/V, the rotated q (written, then read) and the output."""
+        B, T = cls.B, cls.T
+        kv_read = int((KV_TOKEN * (lengths + T)).sum())
+        qkv = B * T * 3 * H * D * 2
+        cs = B * T * (D // 2) * 2 * 4
+        append = B * T * 2 * H * D * 2
+        q_rw = 2 * B * T * H * D * 2
+        out = B * T * H * D * 2
+        attention = kv_read + B * T * H * D * 2 + out  # what draft_attention itself must move
+        return {"layer": kv_read + qkv + cs + append + q_rw + out, "attention": attention}
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        B, T, CAP = self.B, self.T, self.CAP
+        lengths = self.lengths()
+        self.lengths_cpu = lengths
+        self.keys = keys_bucket(int(lengths.max()) + T)
+        self.kc = [self.randn(B, H, CAP, D) for _ in range(self.layers)]
+        self.vc = [self.randn(B, H, CAP, D) for _ in range(self.layers)]
+        self.qkv = self.randn(self.layers, B * T, 3 * H * D)
+        self.cs = rope_table(CAP).to(self.device)
+        self.pos = (lengths[:, None] + torch.arange(T)).reshape(-1).to(self.device)  # positions of the 5 tokens
+        self.slots = torch.arange(B).repeat_interleave(T).to(self.device)
+        self.att_len = (lengths + 1).to(self.device)  # query i of a row sees lengths + 1 + i keys (spec.py:95)
+        nb = self.bytes(lengths)
+        self.step_units = nb["layer"] * self.layers
+        self.roof_units = nb["attention"]
+        self.h2d = [self.qkv]
+
+    def run(self, ev=None):
         outs = []
-        for i in range(LAYERS):
+        for i in range(self.layers):
             q = self.K.rope_kv(self.qkv[i], self.cs, self.pos, self.kc[i], self.vc[i], H, self.slots)
-            if timed_events:
-                self.ev[i][0].record()
-            outs.append(self.K.draft_attention(q, self.kc[i], self.vc[i], self.att_len, T, self.keys, self.scale))
-            if timed_events:
-                self.ev[i][1].record()
+            if ev:
+                ev[i][0].record()
+            outs.append(self.K.draft_attention(q, self.kc[i], self.vc[i], self.att_len, self.T, self.keys, D**-0.5))
+            if ev:
+                ev[i][1].record()
+        self.d2h = outs
         return outs
 
-    def capture(self):
-        self.ev = [(torch.cuda.Event(enable_timing=True, external=True),
-                    torch.cuda.Event(enable_timing=True, external=True)) for _ in range(LAYERS)]
-        s = torch.cuda.Stream(self.device)
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
-            self.run()  # warm-up outside the capture (the appended K/V are rewritten identically)
-            torch.cuda.synchronize(self.device)
-            self.graph = torch.cuda.CUDAGraph()
-            self.graph.capture_begin()
-            self.outs = self.run(timed_events=True)
-            self.graph.capture_end()
-        torch.cuda.current_stream(self.device).wait_stream(s)
-        torch.cuda.synchronize(self.device)
+    def config(self):
+        return {"workload": "BASELINE config 2: spec-4 verify attention + fused RoPE/KV append, batch 8 per GPU, "
+                            "T=5, 32x128 heads, lengths U[200,2000], cache 4096, 12 layers per step",
+                "global_batch": self.B * self.world, "q_len": self.T, "heads": H, "head_dim": D,
+                "layers": self.layers, "keys_bucket": self.keys, "bytes_per_step_per_gpu": self.step_units,
+                "l2": "inputs larger than L2: each step reads 12 distinct layer caches (~1.7 GB)"}
 
-    def attention_ms(self) -> list[float]:
-        """Per-layer duration of the verify attention in the last replay (CUDA events inside the graph)."""
-        return [a.elapsed_time(b) for a, b in self.ev]
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import attention as oatt
+        from oracle import rope as orope
+
+        B, T = cls.B, cls.T
+        lengths = cls.lengths()
+        keys = keys_bucket(int(lengths.max()) + T)
+        g = cpu_gen(1)
+        kc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
+        vc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
+        qkv = torch.randn(B * T, 3 * H * D, generator=g).to(torch.bfloat16)
+        cs = orope.rope_table(D, cls.CAP).numpy()
+        pos = (lengths[:, None] + torch.arange(T)).reshape(-1).numpy()
+        slots = np.repeat(np.arange(B), T)
+        kn = kc.view(torch.int16).numpy().view(np.uint16)
+        vn = vc.view(torch.int16).numpy().view(np.uint16)
+        qkv_raw = qkv.view(torch.int16).numpy().view(np.uint16)
+
+        def one():
+            qn = orope.rope_kv(qkv_raw, cs, pos, kn, vn, H, slots, None, True)
+            q = torch.from_numpy(qn.astype(np.int16)).view(torch.bfloat16)
+            oatt.draft_attention_model_dtype(q, kc, vc, lengths + 1, T, D**-0.5)
+            return cls.bytes(lengths)["layer"]
+
+        return one, ("1 of the 12 layers of a step (B=8, T=5, 32x128, same lengths): oracle RoPE/append (numpy) + "
+                     "model-dtype verify attention (torch CPU)")
+
+
+class Decode(Workload):
+    """q_len-1 decode attention, batch 8, 1024 keys per row (12 layer caches, > L2)."""
+
+    name = "decode"
+    metric = "decode-attn HBM GB/s (q_len 1, batch 8, 1024 keys, 12 layers)"
+    roof_kernel = "decode_attention (split + combine launches of one layer)"
+    traffic_key = "decode_attention_config1_bytes_per_call"
+    B, L = 8, 1024
+    calls_per_layer = 2
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        B, L = self.B, self.L
+        self.kc = [self.randn(B, H, L, D) for _ in range(self.layers)]
+        self.vc = [self.randn(B, H, L, D) for _ in range(self.layers)]
+        self.q = self.randn(self.layers, B, H, D)
+        self.lengths = torch.full((B,), L, dtype=torch.int64, device=self.device)
+        self.roof_units = B * L * KV_TOKEN + 2 * B * H * D * 2
+        self.step_units = self.roof_units * self.layers
+        self.h2d = [self.q]
+
+    def run(self, ev=None):
+        outs = []
+        for i in range(self.layers):
+            if ev:
+                ev[i][0].record()
+            outs.append(self.K.decode_attention(self.q[i], self.kc[i], self.vc[i], self.lengths, self.L, D**-0.5))
+            if ev:
+                ev[i][1].record()
+        self.d2h = outs
+        return outs
+
+    def config(self):
+        return {"workload": "BASELINE config 1: decode attention, batch 8 per GPU, q_len 1, 32x128 heads, 1024 keys "
+                            "per row, scale 1/sqrt(128), 12 layer caches per step",
+                "global_batch": self.B * self.world, "q_len": 1, "heads": H, "head_dim": D, "layers": self.layers,
+                "bytes_per_step_per_gpu": self.step_units, "l2": "inputs larger than L2 (12 x 134 MB per step)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import attention as oatt
+
+        g = cpu_gen(0)
+        q = torch.randn(cls.B, H, D, generator=g).to(torch.bfloat16)
+        kc = torch.randn(cls.B, H, cls.L, D, generator=g).to(torch.bfloat16)
+        vc = torch.randn(cls.B, H, cls.L, D, generator=g).to(torch.bfloat16)
+        lengths = torch.full((cls.B,), cls.L, dtype=torch.int64)
+
+        def one():
+            oatt.draft_attention_model_dtype(q, kc, vc, lengths, 1, D**-0.5)
+            return cls.B * cls.L * KV_TOKEN + 2 * cls.B * H * D * 2
+
+        return one, "one decode-attention call (B=8, 1024 keys, 32x128): model-dtype masked softmax (torch CPU)"
+
+
+class Beam(Workload):
+    """BASELINE config 3 (attention): 8 inputs x 5 beams; the context is read once per input."""
+
+    name = "beam"
+    metric = "beam-attn HBM GB/s (8 inputs x 5 beams, context U[300,1800], 12 layers)"
+    roof_kernel = "beam_attention (context, generated and combine launches of one layer)"
+    traffic_key = "beam_attention_config3_bytes_per_call"
+    S, N, CAP, G, GEN = 8, 5, 2048, 64, 32
+    calls_per_layer = 3  # context pass (tensor cores), generated-key pass, combine
+
+    @classmethod
+    def draw(cls):
+        g = cpu_gen(0)
+        ctx = torch.randint(300, 1801, (cls.S,), generator=g)
+        picks = torch.randint(0, cls.N, (cls.S * cls.N, cls.G), generator=g, dtype=torch.int32)
+        ptr = (torch.arange(cls.S * cls.N, dtype=torch.int32)[:, None] // cls.N) * cls.N + picks
+        return ctx, ptr
+
+    @classmethod
+    def bytes(cls, ctx: torch.Tensor) -> int:
+        rows = cls.S * cls.N
+        return int(KV_TOKEN * ctx.sum()) + rows * cls.GEN * KV_TOKEN + rows * cls.GEN * 4 + 2 * rows * H * D * 2
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        S, N, rows = self.S, self.N, self.S * self.N
+        ctx, ptr = self.draw()
+        self.ctx_keys = keys_bucket(int(ctx.max()))
+        self.kc = [self.randn(S, H, self.CAP, D) for _ in range(self.layers)]
+        self.vc = [self.randn(S, H, self.CAP, D) for _ in range(self.layers)]
+        self.kg = [self.randn(rows, H, self.G, D) for _ in range(self.layers)]
+        self.vg = [self.randn(rows, H, self.G, D) for _ in range(self.layers)]
+        self.q = self.randn(self.layers, rows, H, D)
+        self.ctx = ctx.to(self.device)
+        self.ptr = ptr.to(self.device)
+        self.gen_len = torch.full((rows,), self.GEN, dtype=torch.int64, device=self.device)
+        self.roof_units = self.bytes(ctx)
+        self.step_units = self.roof_units * self.layers
+        self.h2d = [self.q]
+
+    def run(self, ev=None):
+        outs = []
+        for i in range(self.layers):
+            if ev:
+                ev[i][0].record()
+            outs.append(self.K.beam_attention(self.q[i], self.kc[i], self.vc[i], self.ctx, self.kg[i], self.vg[i],
+                                              self.ptr, self.gen_len, self.N, self.ctx_keys, D**-0.5))
+            if ev:
+                ev[i][1].record()
+        self.d2h = outs
+        return outs
+
+    def config(self):
+        return {"workload": "BASELINE config 3 (attention): 8 inputs x 5 beams = 40 rows per GPU, q_len 1, 32x128, "
+                            "context U[300,1800] shared per input (read once per input), 32 generated keys per row "
+                            "through int32 pointers, 12 layers",
+                "global_batch": self.S * self.N * self.world, "heads": H, "head_dim": D, "layers": self.layers,
+                "bytes_per_step_per_gpu": self.step_units, "l2": "inputs larger than L2 (12 layers, ~1.5 GB)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import attention as oatt
+
+        ctx, ptr = cls.draw()
+        rows = cls.S * cls.N
+        g = cpu_gen(1)
+        q = torch.randn(rows, H, D, generator=g).to(torch.bfloat16)
+        keys = keys_bucket(int(ctx.max()))
+        kc = torch.randn(cls.S, H, keys, D, generator=g).to(torch.bfloat16)
+        vc = torch.randn(cls.S, H, keys, D, generator=g).to(torch.bfloat16)
+        kg = torch.randn(rows, H, cls.G, D, generator=g).to(torch.bfloat16)
+        vg = torch.randn(rows, H, cls.G, D, generator=g).to(torch.bfloat16)
+        gen_len = torch.full((rows,), cls.GEN, dtype=torch.int64)
+
+        def one():
+            oatt.beam_attention(q, kc, vc, ctx, kg, vg, ptr.long(), gen_len, cls.N, D**-0.5, dtype=torch.float32)
+            return cls.bytes(ctx)
+
+        return one, "one beam-attention call (40 rows, same lengths): per-row fp32 masked softmax (torch CPU)"
+
+
+class Gather(Workload):
+    """BASELINE config 3 (reorder): out[r] = src[parent[r]] over a layer's K and V cache rows, bit-exact."""
+
+    name = "gather"
+    metric = "beam KV reorder HBM GB/s (read + write, 40 rows x [32, 2048, 128] bf16, K and V)"
+    roof_kernel = "reorder_gather (one launch per K or V tensor)"
+    traffic_key = "reorder_gather_config3_bytes_per_call"
+    S, N, CAP = 8, 5, 2048
+    COPIES = 3  # distinct source layers cycled through, so a step never finds its source in L2
+
+    @classmethod
+    def parents(cls) -> torch.Tensor:
+        picks = torch.randint(0, cls.N, (cls.S * cls.N,), generator=cpu_gen(0), dtype=torch.int32)
+        return (torch.arange(cls.S * cls.N, dtype=torch.int32) // cls.N) * cls.N + picks
+
+    def __init__(self, device, rank, world, layers):
+        super().__init__(device, rank, world, min(layers, self.COPIES))
+        rows = self.S * self.N
+        self.src = [(self.randn(rows, H, self.CAP, D), self.randn(rows, H, self.CAP, D)) for _ in range(self.layers)]
+        self.dst = (torch.empty_like(self.src[0][0]), torch.empty_like(self.src[0][1]))
+        self.parent = self.parents().to(self.device)
+        self.row_bytes = H * self.CAP * D * 2
+        self.roof_units = 2 * rows * self.row_bytes  # read + write of one tensor
+        self.step_units = 2 * self.roof_units * self.layers
+        self.h2d = [self.parent]
+        self.calls_per_layer = 2
+
+    def run(self, ev=None):
+        for i in range(self.layers):
+            for t in range(2):
+                if ev and t == 0:
+                    ev[i][0].record()
+                self.K.reorder_gather(self.src[i][t], self.parent, self.dst[t])
+                if ev and t == 0:
+                    ev[i][1].record()
+        self.d2h = [self.dst[0][:, 0, 0, :8]]  # a few bytes of each gathered row: the step's visible result
+        return self.dst
+
+    def config(self):
+        return {"workload": "BASELINE config 3 (reorder): K and V cache rows [40, 32, 2048, 128] bf16 gathered by "
+                            "int32 parents U[0,5) within each input's 5 beams",
+                "rows": self.S * self.N, "row_bytes": self.row_bytes, "source_layers": self.layers,
+                "bytes_per_step_per_gpu": self.step_units,
+                "l2": f"inputs larger than L2 ({self.layers} distinct 671 MB sources per step)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import gather as og
+
+        rows = cls.S * cls.N
+        src = np.random.default_rng(0).integers(0, 65535, (rows, H * cls.CAP * D // 8), dtype=np.uint16)
+        parent = cls.parents().numpy()
+
+        def one():
+            og.reorder_gather(src, parent)
+            return 2 * src.nbytes
+
+        return one, "the reorder of one 40-row tensor at 1/8 of the row length (numpy fancy indexing)"
+
+
+class Prefill(Workload):
+    """BASELINE config 4 (prefill): causal attention of 8 rows x 1500 frames, 12 layers, tensor-bound."""
+
+    name = "prefill"
+    metric = "prefill-attn TFLOP/s (causal, 8 x 1500 frames, 32x128, 12 layers)"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    roof_kernel = "prefill_attention (one launch per layer)"
+    traffic_key = "prefill_attention_config4_bytes_per_call"
+    B, W, CAP = 8, 1500, 2048
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        B, W = self.B, self.W
+        # q as rope_kv returns it ([B*W, H, D]) and k/v as the prefill reads them: cache views (decode.py:156-158)
+        self.q = self.randn(self.layers, B * W, H, D)
+        self.kc = [self.randn(B, H, self.CAP, D) for _ in range(self.layers)]
+        self.vc = [self.randn(B, H, self.CAP, D) for _ in range(self.layers)]
+        self.roof_units = 4 * (W * (W + 1) // 2) * D * B * H  # QK^T and PV over the causal half (incl. diagonal)
+        self.step_units = self.roof_units * self.layers
+        self.h2d = [self.q]
+
+    def run(self, ev=None):
+        outs = []
+        for i in range(self.layers):
+            q = self.q[i].view(self.B, self.W, H, D).transpose(1, 2)
+            if ev:
+                ev[i][0].record()
+            o = self.K.prefill_attention(q, self.kc[i][:, :, :self.W], self.vc[i][:, :, :self.W], D**-0.5)
+            if ev:
+                ev[i][1].record()
+            outs.append(o)
+        self.d2h = outs
+        return outs
+
+    def config(self):
+        return {"workload": "BASELINE config 4 (prefill attention): 8 rows x 1500 frames per GPU, causal, 32x128 "
+                            "heads, q [B*W,H,D] and K/V cache views of capacity 2048, 12 layers",
+                "global_batch": self.B * self.world, "width": self.W, "heads": H, "head_dim": D,
+                "layers": self.layers, "flops_per_step_per_gpu": self.step_units,
+                "l2": "inputs larger than L2 (12 layers x 294 MB of q/k/v per step)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        g = cpu_gen(1)
+        W = cls.W
+        q = torch.randn(1, 8, W, D, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, 8, W, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(1, 8, W, D, generator=g).to(torch.bfloat16)
+
+        def one():
+            torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+            return 4 * (W * (W + 1) // 2) * D * 8
+
+        return one, "one row x 8 heads x 1500 frames: torch SDPA (causal, bf16) on the CPU, the reference's call"
+
+
+class Sweep(Workload):
+    """64 rows sharded over the ranks; q_len 1 and 5 at lengths 512, 2048 and 8192."""
+
+    name = "sweep"
+    metric = "decode-attn HBM GB/s, whole box (64 rows sharded, q_len 1/5, lengths 512/2048/8192)"
+    roof_kernel = "draft_attention (q_len 5, 8192 keys)"
+    traffic_key = "draft_attention_config5_bytes_per_call"
+    ROWS, CASES = 64, [(1, 512), (1, 2048), (1, 8192), (5, 512), (5, 2048), (5, 8192)]
+    calls_per_layer = 2
+
+    def __init__(self, device, rank, world, layers):
+        super().__init__(device, rank, world, len(self.CASES))
+        if self.ROWS % world:
+            raise SystemExit(f"sweep: {self.ROWS} rows do not split over {world} ranks")
+        self.rows = self.ROWS // world
+        self.keys = [L if t == 1 else keys_bucket(L + t) for t, L in self.CASES]
+        cap = max(self.keys)
+        self.kc = self.randn(self.rows, H, cap, D)
+        self.vc = self.randn(self.rows, H, cap, D)
+        self.q = {t: self.randn(self.rows * t, H, D) for t in (1, 5)}
+        self.case_bytes = [self.rows * KV_TOKEN * (L + t - 1) + 2 * self.rows * t * H * D * 2 for t, L in self.CASES]
+        self.roof_units = self.case_bytes[-1]
+        self.step_units = sum(self.case_bytes)
+        self.n = {L: torch.full((self.rows,), L, dtype=torch.int64, device=self.device) for _, L in self.CASES}
+        self.h2d = [self.q[1], self.q[5]]
+
+    def run(self, ev=None):
+        outs = []
+        for i, (t, L) in enumerate(self.CASES):
+            n, keys = self.n[L], self.keys[i]
+            if ev:
+                ev[i][0].record()
+            if t == 1:
+                outs.append(self.K.decode_attention(self.q[1], self.kc, self.vc, n, keys, D**-0.5))
+            else:
+                outs.append(self.K.draft_attention(self.q[5], self.kc, self.vc, n, t, keys, D**-0.5))
+            if ev:
+                ev[i][1].record()
+        self.d2h = outs
+        return outs
+
+    def config(self):
+        return {"workload": "BASELINE config 5: 64 rows in all, sharded evenly over the GPUs, 32x128 heads; cases "
+                            "q_len {1,5} x cached length {512, 2048, 8192}, one call each per step",
+                "rows_per_gpu": self.rows, "cases": [f"q{t}_L{L}" for t, L in self.CASES],
+                "bytes_per_step_per_gpu": self.step_units, "l2": "inputs larger than L2 (every case > 126 MB at 8 "
+                                                                 "rows/GPU except 512 keys: 67 MB, 5 cases after it)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import attention as oatt
+
+        g = cpu_gen(0)
+        rows, L = 8, 2048
+        q = torch.randn(rows * 5, H, D, generator=g).to(torch.bfloat16)
+        kc = torch.randn(rows, H, L + 8, D, generator=g).to(torch.bfloat16)
+        vc = torch.randn(rows, H, L + 8, D, generator=g).to(torch.bfloat16)
+        n = torch.full((rows,), L, dtype=torch.int64)
+
+        def one():
+            oatt.draft_attention_model_dtype(q, kc, vc, n, 5, D**-0.5)
+            return rows * KV_TOKEN * (L + 4) + 2 * rows * 5 * H * D * 2
+
+        return one, "8 rows, q_len 5, 2048 keys (one case of the sweep): model-dtype masked softmax (torch CPU)"
+
+
+WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep)}
+
+
+# --------------------------------------------------------------------------------------------------------- timing
 
 
 class Clocks:
@@ -172,52 +584,20 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def traffic_per_launch() -> float | None:
-    """DRAM bytes per verify-attention call from the committed ncu summary, if one is present."""
-    path = ROOT / "profiles" / "roofline_traffic.txt"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        if line.startswith("draft_attention_config2_bytes_per_call="):
-            return float(line.split("=", 1)[1])
-    return None
-
-
-def cpu_baseline(seconds: float = 10.0) -> dict:
-    """The CPU port of the reference's path (oracle) on one layer of the same workload, on all host cores."""
-    from oracle import attention as oatt
-    from oracle import rope as orope
-
+def cpu_time(wl, seconds: float) -> dict:
+    """The CPU port of the reference's path (oracle) on a bounded sample of the workload, on all host cores."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    lengths = workload_lengths()
-    keys = keys_bucket(lengths)
-    g = torch.Generator().manual_seed(1)
-    kc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
-    vc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
-    qkv = torch.randn(B * T, 3 * H * D, generator=g).to(torch.bfloat16)
-    cs = orope.rope_table(D, CAP).numpy()
-    pos = (lengths[:, None] + torch.arange(T)).reshape(-1).numpy()
-    slots = np.repeat(np.arange(B), T)
-    kn = kc.view(torch.int16).numpy().view(np.uint16)
-    vn = vc.view(torch.int16).numpy().view(np.uint16)
-    qkv_raw = qkv.view(torch.int16).numpy().view(np.uint16)
-    nbytes = algorithmic_bytes(lengths)["layer"]
-
-    def one():
-        qn = orope.rope_kv(qkv_raw, cs, pos, kn, vn, H, slots, None, True)
-        q = torch.from_numpy(qn.astype(np.int16)).view(torch.bfloat16)
-        oatt.draft_attention_model_dtype(q, kc, vc, lengths + 1, T, D**-0.5)
-
+    one, sample = wl.cpu_sampler()
     one()
-    reps, t0 = 0, time.perf_counter()
+    reps, units, t0 = 0, 0.0, time.perf_counter()
     while time.perf_counter() - t0 < seconds or reps < 3:
-        one()
+        units += one()
         reps += 1
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"1 of the 12 layers of a step (B=8, T=5, 32x128, same lengths), {reps} repetitions over "
-                      f"{seconds:.0f} s: oracle RoPE/append (numpy) + model-dtype verify attention (torch CPU)"}
+    dt = time.perf_counter() - t0
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    return {"value": round(units / dt / scale, 3), "unit": wl.unit, "cores": threads, "kind": "port",
+            "sample": f"{sample}; {reps} repetitions in {dt:.1f} s"}
 
 
 def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -225,10 +605,21 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    step = Step(device, seed=1000 + rank)
-    step.capture()
-    nbytes = algorithmic_bytes(step.lengths_cpu)
-    step_bytes = nbytes["layer"] * LAYERS
+    wl = WORKLOADS[args.workload](device, rank, world, args.layers)
+    n_ev = wl.layers
+    ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+          for _ in range(n_ev)]
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        wl.run()  # warm-up outside the capture (plans, tensor maps, appended rows rewritten identically)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        graph.capture_begin()
+        wl.run(ev)
+        graph.capture_end()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
 
     def barrier():
         if world > 1:
@@ -243,7 +634,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # --- device-resident timing (value) ---
     for _ in range(args.warmup):
-        step.graph.replay()
+        graph.replay()
     torch.cuda.synchronize(device)
     clocks = Clocks(device.index) if rank == 0 else None
     barrier()
@@ -251,26 +642,29 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
-        step.graph.replay()
+        graph.replay()
     end.record()
     torch.cuda.synchronize(device)
     barrier()
     clock = clocks.stop() if clocks else None
     ms = max_over_ranks(start.elapsed_time(end))
-    att_ms = step.attention_ms()  # the last timed step's per-layer verify attention
-    att_ms = max_over_ranks(float(np.mean(att_ms)))
+    per_call = [a.elapsed_time(b) for a, b in ev]  # the last timed step's dominant calls
+    roof_ms = max_over_ranks(float(np.mean(per_call)) if args.workload != "sweep" else per_call[-1])
+    case_ms = [max_over_ranks(x) for x in per_call] if args.workload == "sweep" else None
 
-    # --- end to end through the public API: host qkv in, outputs back to the host, every step ---
-    qkv_host = torch.empty_like(step.qkv, device="cpu").pin_memory()
-    qkv_host.copy_(step.qkv.cpu())
-    out_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in step.outs]
+    # --- end to end through the public API: inputs from pinned host memory, results back, every step ---
+    hosts_in = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in wl.h2d]
+    for h, t in zip(hosts_in, wl.h2d):
+        h.copy_(t.cpu())
+    hosts_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in wl.d2h]
     stream = torch.cuda.current_stream(device)
 
     def e2e_step():
-        step.qkv.copy_(qkv_host, non_blocking=True)
-        step.graph.replay()
-        for h, o in zip(out_host, step.outs):
-            h.copy_(o, non_blocking=True)
+        for h, t in zip(hosts_in, wl.h2d):
+            t.copy_(h, non_blocking=True)
+        graph.replay()
+        for h, t in zip(hosts_out, wl.d2h):
+            h.copy_(t, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -287,38 +681,42 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if rank != 0:
         return None
-    peak, peak_kind = peaks()
+    pk = peaks()
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    peak = pk["tensor"] if wl.bound == "tensor" else pk["hbm"]
     ms_step = ms / args.steps
-    value = world * step_bytes / (ms_step * 1e-3) / 1e9
-    achieved = nbytes["attention"] / (att_ms * 1e-3) / 1e9
-    traffic = traffic_per_launch()
+    value = world * wl.step_units / (ms_step * 1e-3) / scale
+    achieved = wl.roof_units / (roof_ms * 1e-3) / scale
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 caches and qkv; lengths seed 0)",
-        "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
-        "config": {"workload": "BASELINE config 2: spec-4 verify attention + fused RoPE/KV append, batch 8 per GPU, "
-                               "T=5, 32x128 heads, lengths U[200,2000], cache 4096, 12 layers per step",
-                   "global_batch": B * world, "q_len": T, "heads": H, "head_dim": D, "layers": LAYERS,
-                   "keys_bucket": step.keys, "bytes_per_step_per_gpu": step_bytes,
-                   "l2": "inputs larger than L2: each step reads 12 distinct layer caches (~1.7 GB)",
-                   "parallelism": f"request-sharded dp{world} (no collective)"},
-        "e2e": {"value": round(world * step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "sweep" else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 tensors; lengths and parents from the seed-0 CPU generator)",
+        "config": dict(wl.config(), parallelism=f"request-sharded dp{world} (no collective)"),
+        "e2e": {"value": round(world * wl.step_units / (e2e_ms / args.steps * 1e-3) / scale, 1), "unit": wl.unit,
                 "ms_per_step": round(e2e_ms / args.steps, 4),
-                "h2d_bytes_per_step": int(qkv_host.numel() * qkv_host.element_size()),
-                "d2h_bytes_per_step": int(sum(o.numel() * o.element_size() for o in out_host)),
-                "path": "kernels.rope_kv + kernels.draft_attention captured in a CUDA graph; pinned host qkv copied "
-                        "in and every layer's output copied out each step"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 3), "peak_kind": peak_kind,
-                     "kernel": "draft_attention (split + combine launches of one layer)",
-                     "traffic": traffic, "bytes_per_launch": nbytes["attention"],
-                     "us_per_launch": round(att_ms * 1e3, 2)},
-        "gpu_launches": 3 * LAYERS * args.steps,
+                "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in hosts_in)),
+                "d2h_bytes_per_step": int(sum(t.numel() * t.element_size() for t in hosts_out)),
+                "path": "omniasr_b200.kernels calls captured in a CUDA graph; inputs copied in from pinned host "
+                        "memory and results copied out every step"},
+        "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "TFLOP/s" if wl.bound == "tensor" else "GB/s", "frac": round(achieved / peak, 3),
+                     "peak_kind": pk["kind"], "kernel": wl.roof_kernel, "traffic": traffic_per_launch(wl.traffic_key),
+                     ("flops_per_launch" if wl.bound == "tensor" else "bytes_per_launch"): wl.roof_units,
+                     "us_per_launch": round(roof_ms * 1e3, 2)},
+        "gpu_launches": wl.launches_per_step() * args.steps,
         "clocks": clock,
     }
-    if world == 1:
-        line["cpu_baseline"] = cpu_baseline()
+    if wl.unit == "GB/s":
+        line["pct_of_8tbs"] = round(100 * value / world / NOMINAL_HBM_GBS, 1)
+    if case_ms is not None:
+        line["cases"] = {f"q{t}_L{L}": {"per_gpu_gbs": round(b / (c * 1e-3) / 1e9, 1),
+                                        "box_gbs": round(world * b / (c * 1e-3) / 1e9, 1), "us": round(c * 1e3, 1)}
+                         for (t, L), b, c in zip(wl.CASES, wl.case_bytes, case_ms)}
+    if args.layers != LAYERS and args.workload not in ("sweep", "gather"):
+        line["config"]["reduced"] = f"{args.layers} of {LAYERS} layers (profiling case, not a headline number)"
+    if world == 1 and args.cpu_seconds > 0:
+        line["cpu_baseline"] = cpu_time(WORKLOADS[args.workload], args.cpu_seconds)
     return line
 
 
@@ -329,45 +727,25 @@ def run_reference(args, rank: int) -> dict | None:
     """The CPU port of the reference's algorithm (oracle), on all host cores, rank 0 only."""
     if rank != 0:
         return None
-    from oracle import attention as oatt
-    from oracle import rope as orope
-
+    wl = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    lengths = workload_lengths()
-    keys = keys_bucket(lengths)
-    g = torch.Generator().manual_seed(1)
-    kc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
-    vc = torch.randn(B, H, keys, D, generator=g).to(torch.bfloat16)
-    qkv = torch.randn(B * T, 3 * H * D, generator=g).to(torch.bfloat16)
-    cs = orope.rope_table(D, CAP).numpy()
-    pos = (lengths[:, None] + torch.arange(T)).reshape(-1).numpy()
-    slots = np.repeat(np.arange(B), T)
-    kn = kc.view(torch.int16).numpy().view(np.uint16)
-    vn = vc.view(torch.int16).numpy().view(np.uint16)
-    qkv_raw = qkv.view(torch.int16).numpy().view(np.uint16)
-
-    def one_layer():
-        qn = orope.rope_kv(qkv_raw, cs, pos, kn, vn, H, slots, None, True)
-        q = torch.from_numpy(qn.astype(np.int16)).view(torch.bfloat16)
-        return oatt.draft_attention_model_dtype(q, kc, vc, lengths + 1, T, D**-0.5)
-
+    one, sample = wl.cpu_sampler()
     for _ in range(args.warmup):
-        one_layer()
-    t0 = time.perf_counter()
+        one()
+    units, t0 = 0.0, time.perf_counter()
     for _ in range(args.steps):
-        one_layer()
-    dt = (time.perf_counter() - t0) / args.steps
-    value = algorithmic_bytes(lengths)["layer"] / dt / 1e9
-    sample = "one layer of the step per timed iteration (B=8, T=5, 32x128, same lengths); GB/s is size-independent"
-    return {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 2 (one layer per step on the CPU)", "global_batch": B,
-                       "q_len": T, "heads": H, "head_dim": D},
-            "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+        units += one()
+    dt = time.perf_counter() - t0
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = units / dt / scale
+    return {"impl": "reference", "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{wl.name}: bounded CPU sample per step ({sample})"},
+            "cpu_baseline": {"value": round(value, 3), "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": sample},
-            "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 3), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
@@ -376,6 +754,9 @@ def main():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="verify")
+    p.add_argument("--layers", type=int, default=LAYERS)
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length (0: none)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

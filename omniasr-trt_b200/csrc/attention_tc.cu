@@ -6,12 +6,15 @@
 // every SM streams the same number of K/V bytes whatever the ragged lengths. A unit cut between CTAs leaves one
 // partial (max, sum, unnormalised output) per CTA ("segment"); the combine kernel merges the segments of a unit.
 //
-// One CTA: warp 4 is the TMA producer (K and V tiles, two 64-column boxes each, 128-byte swizzle, into a ring of
-// six 32 KB slots: three tiles in flight); warps 0-3 are the consumers, thread t owning TMEM lane t:
+// One CTA (256 threads): warp 4 loads the queries and the K tiles, warp 6 the V tiles (TMA, two 64-column boxes
+// each, 128-byte swizzle, three 32 KB slots per operand); warp 5 issues the MMAs; warps 0-3 run the softmax,
+// thread t owning TMEM lane t; warp 7 writes finished units out:
 //   S^T[128 keys x 16 q]  = K_tile [128 x 128] . Q^T         (tcgen05.mma, M=128 N=16, K-major A and B)
 //   softmax over the keys of each query column (online, fp32, log2 units), P^T written to shared memory (bf16)
 //   O^T[128 dims x 16 q]  = V_tile^T [128 x 128 keys] . P^T   (M=128 N=16, MN-major A and B)
-// The per-tile O^T is read back from TMEM and accumulated in registers (thread t = head dim t).
+// The per-tile O^T is read back from TMEM one tile later and accumulated in registers (thread t = head dim t);
+// a unit's accumulator goes through a shared-memory stash to warp 7, so a unit boundary costs the softmax warps
+// no global stores. The set-up before griddepcontrol.wait overlaps the previous kernel (programmatic launch).
 //
 // Algorithm of the reference restated: omniasr_trt/kernels.py:56-113 (_beam_ctx, CAUSAL for drafts) and
 // kernels.py:163-195 (_attn_split): the same online softmax per split, merged by the combine
@@ -42,10 +45,13 @@ template <int SLOTS>
 struct Smem {
   static constexpr int Q_OFF = SLOTS * SLOT_BYTES;      // two query buffers (units u and u + 1), 4 KB each
   static constexpr int P_OFF = Q_OFF + 2 * NQP * D * 2;
-  static constexpr int RED_OFF = P_OFF + 2 * NQP * BN * 2;
-  static constexpr int BYTES = RED_OFF + 4 * NQP * 4 + 1024;  // + alignment slack
+  static constexpr int RED_OFF = P_OFF + 2 * NQP * BN * 2;         // column maxima of the 4 softmax warps
+  static constexpr int RED_L_OFF = RED_OFF + 4 * NQP * 4;           // column sums of a finished unit
+  static constexpr int STASH_M_OFF = RED_L_OFF + 4 * NQP * 4;       // its running max per column
+  static constexpr int STASH_OFF = STASH_M_OFF + NQP * 4;           // its accumulator [NQP][128 dims]
+  static constexpr int BYTES = STASH_OFF + NQP * D * 4 + 1024;      // + alignment slack
 };
-constexpr int THREADS = 224;  // warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads
+constexpr int THREADS = 256;  // warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads, 7 write-out
 constexpr uint32_t TMEM_COLS = 64;  // S^T x2 (cols 0-31), O^T x2 (cols 32-63)
 constexpr uint32_t IDESC_S = idesc_bf16(128, NQP, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(128, NQP, 1, 1);
@@ -254,6 +260,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[SLOTS], empty[SLOTS];
   __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_fill[2], q_done[2], drain;
+  __shared__ __align__(8) uint64_t seg_ready, seg_free;  // the stash holds a finished unit / was written out
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ volatile int issued_k, issued_v, q_issued;  // K / V tiles and query tiles the producers issued
@@ -262,28 +269,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  // The lengths, read by every role's walk, once into shared memory.
-  __shared__ int64_t s_len[kSmemGroups];
-  Params p = pin;
-  if (p.groups <= kSmemGroups) {
-    for (int g = tid; g < p.groups; g += THREADS) s_len[g] = pin.lengths[g];
-    __syncthreads();
-    p.lengths = s_len;
-  }
-
-  const int64_t total = total_cost(p);
-  // At least one tile's cost per CTA, so that every CTA between a unit's first and last owns one of its tiles.
-  const int64_t per = max((total + gridDim.x - 1) / gridDim.x, kTileCost);
-  const int64_t c0 = (int64_t)blockIdx.x * per;
-  const int64_t c1 = min(total, c0 + per);
-  {
-    TileIter probe;
-    probe.init(p, c0, c1);
-    if (c0 >= c1 || probe.done) return;  // no tile for this CTA (uniform)
-  }
-  OMNI_TRACE_CTA(0);
-
+  // Set-up that reads nothing an earlier kernel writes: barriers, TMEM, the tensor maps. Launched as a
+  // programmatic dependent, this overlaps the previous kernel's tail.
   if (tid == 0) {
+    OMNI_TRACE_AT(4002);
     for (int s = 0; s < SLOTS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -300,15 +289,46 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&q_done[s], 1);
     }
     mbar_init(&drain, 1);
+    mbar_init(&seg_ready, 128);
+    mbar_init(&seg_free, 1);
     mbar_fence_init();
     abort_flag = 0;
     issued_k = issued_v = q_issued = 0;
   }
-  if (tid == 0) OMNI_TRACE_AT(4000);
   if (warp == 0) tmem_alloc(&tmem_base, TMEM_COLS);
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&qmap);
+  }
+  if (warp == 6 && lane == 0) prefetch_tmap(&vmap);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0) OMNI_TRACE_AT(4000);
+  // The queries, the cache rows and the lengths may come from the kernel before this one.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // The lengths, read by every role's walk, once into shared memory.
+  __shared__ int64_t s_len[kSmemGroups];
+  Params p = pin;
+  if (p.groups <= kSmemGroups) {
+    for (int g = tid; g < p.groups; g += THREADS) s_len[g] = pin.lengths[g];
+    __syncthreads();
+    p.lengths = s_len;
+  }
+  if (tid == 0) OMNI_TRACE_AT(4003);
+
+  const int64_t total = total_cost(p);
+  if (tid == 0) OMNI_TRACE_AT(4007);
+  // At least one tile's cost per CTA, so that every CTA between a unit's first and last owns one of its tiles.
+  const int64_t per = max((total + gridDim.x - 1) / gridDim.x, kTileCost);
+  const int64_t c0 = (int64_t)blockIdx.x * per;
+  const int64_t c1 = min(total, c0 + per);
+  TileIter first_tile;  // this CTA's first tile; every role starts its walk from a copy
+  first_tile.init(p, c0, c1);
+  const bool has_work = c0 < c1 && !first_tile.done;  // uniform over the CTA
+  if (tid == 0) OMNI_TRACE_AT(4008);
+  OMNI_TRACE_CTA(0);
   if (tid == 0) {
     OMNI_TRACE_AT(4001);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the combine may start its prologue
@@ -317,17 +337,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   unsigned char* qs = smem + L::Q_OFF;
 
   constexpr int HALF = SLOTS / 2;
-  if (warp == 4 || warp == 6) {
+  if (!has_work) {
+    // nothing to do but give the TMEM back
+  } else if (warp == 4 || warp == 6) {
     // ------------------------------------------------------------------ producers: K (+ queries) and V
     if (lane == 0) {
       const bool is_k = warp == 4;
       const CUtensorMap* map = is_k ? &kmap : &vmap;
-      prefetch_tmap(map);
-      if (is_k) prefetch_tmap(&qmap);
-      TileIter ti, ahead;  // `ahead` runs p.prefetch tiles in front: those go to L2 early, beyond the ring
-      ti.init(p, c0, c1);
-      ahead.init(p, c0, c1);
+      TileIter ti = first_tile, ahead = first_tile;  // `ahead` runs p.prefetch tiles in front (into L2 early)
       for (int i = 0; i < p.prefetch && !ahead.done; ++i) ahead.advance();
+      if (is_k) OMNI_TRACE_AT(4005);
       int unit = 0;
       for (int it = 0; !ti.done && !abort_flag; ++it, ti.advance()) {
         const int h = ti.h, tt = ti.t;
@@ -347,6 +366,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_3d(qs + qb * (NQP * D * 2), &qmap, 0, h, ti.g * p.nq, &q_fill[qb]);
           tma_load_3d(qs + qb * (NQP * D * 2) + NQP * 128, &qmap, 64, h, ti.g * p.nq, &q_fill[qb]);
           q_issued = ++unit;
+          if (unit == 1) OMNI_TRACE_AT(4006);
         }
         const int slot = (is_k ? 0 : HALF) + it % HALF, use = it / HALF;
         if (use >= 1 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
@@ -369,8 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      TileIter ti;
-      ti.init(p, c0, c1);
+      TileIter ti = first_tile;
       int unit = -1;
       auto scores = [&](int t) -> bool {  // S^T(t) = K(t) Q^T
         const int b = t & 1, u = t >> 1;
@@ -397,18 +416,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_commit(&empty[slot]);
         return true;
       };
-      // Within a unit, tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1)
-      // runs; at a unit boundary O^T(t-1) goes first (the softmax needs it to finish the unit).
+      // Tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1) runs -- also
+      // across a unit boundary, where the softmax finishes the old unit one tile late.
       bool ok = true;
       int pend = -1;  // tile whose O^T is still to issue
       for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
         if (ti.t == 0 || it == 0) {
-          if (pend >= 0) {
-            ok = values(pend);
-            pend = -1;
-          }
           ++unit;
-          if (ok && !mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
+          if (!mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
         }
         if (ok) ok = scores(it);
         if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
@@ -419,19 +434,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) abort_flag = 1;
     }
     __syncwarp();
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------------ softmax (128 threads, TMEM lane = tid)
     // The running max of a column is raised only when a score passes it by 2^8, so the cross-thread max (and the
     // rescale of the accumulators) is rare; O^T of a tile is accumulated one tile later.
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     float* red = reinterpret_cast<float*>(smem + L::RED_OFF);
-    TileIter ti;
-    ti.init(p, c0, c1);
+    TileIter ti = first_tile;
+    float* red_l = reinterpret_cast<float*>(smem + L::RED_L_OFF);
+    float* stash_m = reinterpret_cast<float*>(smem + L::STASH_M_OFF);
+    float* stash = reinterpret_cast<float*>(smem + L::STASH_OFF);
     float m[NQT], lpart[NQT], acc[NQT], scl[NQT];
     int lim[NQT];
     int g = 0, h = 0, need = 0, tiles = 1;
     int64_t unit_pos0 = 0;
     bool pending = false;
+    bool stashed = false;  // a finished unit waits for its last O^T (read at the next tile)
+    int segs = 0;          // finished units handed to the write-out warp
     for (int it = 0; !ti.done; ++it, ti.advance()) {
       const int tt = ti.t;
       const int b = it & 1;
@@ -538,7 +557,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&p_full[b]);
       if (tid == 0) OMNI_TRACE_AT(it * 8 + 5);
 
-      // The previous tile's O^T, brought to this tile's max.
+      // The previous tile's O^T: brought to this tile's max -- or, when the previous tile ended a unit, added to
+      // that unit's stashed accumulator, which then becomes the unit's segment (or output).
       if (pending) {
         if (!mbar_wait(&o_full[b ^ 1], ((it - 1) >> 1) & 1)) abort_flag = 1;
         if (tid == 0) OMNI_TRACE_AT(it * 8 + 6);
@@ -548,50 +568,98 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld16(tbase + lane_off + 2 * NQP + (b ^ 1) * NQP, o);
         tc_fence_before();
         mbar_arrive(&o_free[b ^ 1]);
+        if (stashed) {
 #pragma unroll
-        for (int j = 0; j < NQT; ++j) acc[j] = fmaf(scl[j], o[j], acc[j]);
+          for (int j = 0; j < NQT; ++j) stash[j * D + tid] += o[j];
+          mbar_arrive(&seg_ready);  // the write-out warp takes it from here
+          ++segs;
+          stashed = false;
+        } else {
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) acc[j] = fmaf(scl[j], o[j], acc[j]);
+        }
       }
       pending = true;
 
       if (last) {
-        // End of this CTA's part of the unit: this tile's O^T, then the unit's segment (or its output).
-        if (!mbar_wait(&o_full[b], par)) abort_flag = 1;
-        tc_fence_after();
-        __syncwarp();
-        float o[NQP];
-        tmem_ld16(tbase + lane_off + 2 * NQP + b * NQP, o);
-        tc_fence_before();
-        mbar_arrive(&o_free[b]);
-#pragma unroll
-        for (int j = 0; j < NQT; ++j) acc[j] += o[j];
-        pending = false;
+        // End of this CTA's part of the unit: its column sums, maximum and accumulator go to the stash once the
+        // write-out warp is done with the previous unit; its last O^T is added one tile later when this CTA has
+        // more tiles (at once otherwise), and the write-out warp turns the stash into the segment (or output).
+        if (segs >= 1 && !mbar_wait_or(&seg_free, (segs - 1) & 1, &abort_flag)) abort_flag = 1;
         {
           int col;
           const float v = butterfly<NQT, false>(lpart, lane, col);
-          if (butterfly_writer<NQT>(lane)) red[warp * NQP + col] = v;
+          if (butterfly_writer<NQT>(lane)) red_l[warp * NQP + col] = v;
         }
-        named_sync(1, 128);
-        const int seg = (int)(blockIdx.x - unit_pos0 / per);
-        const bool whole = (unit_pos0 + kTileCost * (tiles - 1)) / per == unit_pos0 / per;
+        if (tid == 0) {
 #pragma unroll
-        for (int j = 0; j < NQT; ++j) {
-          if (j < p.nq) {
-            const float l = red[j] + red[NQP + j] + red[2 * NQP + j] + red[3 * NQP + j];
-            const int64_t rowh = ((int64_t)g * p.nq + j) * p.heads + h;
-            if (whole && p.out) {
-              p.out[rowh * D + tid] = __float2bfloat16_rn(l > 0.f ? acc[j] / l : 0.f);
-            } else {
-              const int64_t part = rowh * p.st + seg;
-              p.part_o[part * D + tid] = acc[j];
-              if (tid == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(m[j], l);
-            }
-          }
+          for (int j = 0; j < NQT; ++j) stash_m[j] = m[j];  // the same in every thread
         }
-        named_sync(1, 128);
+        TileIter nx = ti;
+        nx.advance();
+        if (!nx.done) {
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) stash[j * D + tid] = acc[j];
+          stashed = true;
+        } else {
+          if (!mbar_wait(&o_full[b], par)) abort_flag = 1;
+          tc_fence_after();
+          __syncwarp();
+          float o[NQP];
+          tmem_ld16(tbase + lane_off + 2 * NQP + b * NQP, o);
+          tc_fence_before();
+          mbar_arrive(&o_free[b]);
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) stash[j * D + tid] = acc[j] + o[j];
+          pending = false;
+          mbar_arrive(&seg_ready);
+          ++segs;
+        }
+        if (tid == 0) OMNI_TRACE_AT(4010 + (it & 7));
       }
+    }
+  } else if (warp == 7) {
+    // ------------------------------------------------------------------ write-out of finished units
+    // Walks this CTA's tiles like the other roles; at a unit's last tile here, waits for the softmax warps'
+    // stash and writes the unit's segment (or output row): lane l holds dimensions 4l .. 4l+3.
+    const float* red_l = reinterpret_cast<const float*>(smem + L::RED_L_OFF);
+    const float* stash_m = reinterpret_cast<const float*>(smem + L::STASH_M_OFF);
+    const float* stash = reinterpret_cast<const float*>(smem + L::STASH_OFF);
+    int segs = 0;
+    for (TileIter ti = first_tile; !ti.done; ti.advance()) {
+      if (!ti.last_here()) continue;
+      if (!mbar_wait_or(&seg_ready, segs & 1, &abort_flag)) {
+        abort_flag = 1;
+        break;
+      }
+      const int64_t pos0 = ti.unit_pos0();
+      const int seg = (int)(blockIdx.x - pos0 / per);
+      const bool whole = (pos0 + kTileCost * (ti.tiles - 1)) / per == pos0 / per;
+      for (int j = 0; j < p.nq && j < NQT; ++j) {
+        const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
+        const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
+        const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
+        if (whole && p.out) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x * inv, a.y * inv);
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z * inv, a.w * inv);
+          uint2 w;
+          w.x = *reinterpret_cast<const uint32_t*>(&lo);
+          w.y = *reinterpret_cast<const uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(p.out + rowh * D + 4 * lane) = w;
+        } else {
+          const int64_t part = rowh * p.st + seg;
+          *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
+          if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&seg_free);
+      ++segs;
     }
   }
   __syncthreads();
+  if (tid == 0) OMNI_TRACE_AT(4020);
   if (abort_flag) {
     if (tid == 0) raise_status(p.status, kStatusTimeout);
     if (tid == 5 * 32) {
@@ -613,6 +681,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }
+  if (tid == 0) OMNI_TRACE_AT(4021);
   OMNI_TRACE_CTA(1);
 }
 
@@ -656,8 +725,10 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   }
   const long long per = max((total + grid - 1) / grid, (long long)kTileCost);
   const int nseg = tiles > 0 ? (int)((pos0 + kTileCost * (tiles - 1)) / per - pos0 / per + 1) : 0;
+  // The pass (and its partials) complete -- waited for by every block, so that the combine's completion implies
+  // the pass's even when the pass finished every unit itself.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (nseg == 1 && extra_ml == nullptr && p.out != nullptr) return;  // finished by the pass
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the pass (and its partials) complete
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + rh * p.st;
   const float2* ml2 = extra_ml ? reinterpret_cast<const float2*>(extra_ml) + rh * extra_st : nullptr;
   // Segments that saw no key (sum 0) take no part, whatever their max.
@@ -787,8 +858,18 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
     if (e != cudaSuccess) return e;
     configured[ci] = true;
   }
-  kern<<<p.grid, THREADS, bytes, stream>>>(kmap, vmap, qmap, p);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the set-up above griddepcontrol.wait overlaps the previous kernel.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = (size_t)bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, p);
 }
 
 cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o, const float* extra_ml, int extra_st,

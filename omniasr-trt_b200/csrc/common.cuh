@@ -76,6 +76,17 @@ OMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// As mbar_wait, but also gives up (false) once *stop is set -- for a role that waits on another role which may
+// have abandoned its work.
+OMNI_DEV bool mbar_wait_or(uint64_t* bar, uint32_t parity, const volatile int* stop) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*stop || global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
 OMNI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -128,5 +139,26 @@ OMNI_DEV float ex2(float x) {
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
+
+// Launches `kern` as a programmatic dependent of the stream's previous kernel: its blocks may start while that
+// kernel drains, and must execute griddepcontrol.wait before reading anything an earlier kernel wrote.
+template <typename Kern, typename... Args>
+inline cudaError_t launch_dependent(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                    Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+OMNI_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+OMNI_DEV void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace omni

@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (tid == 0) OMNI_TRACE_AT(4001);
+  grid_dependency_wait();  // q, k, v may come from the kernel before (launched as a programmatic dependent)
   const uint32_t tbase = tmem_base;
   unsigned char* qs = smem + Q_OFF;
 
@@ -492,8 +493,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   int grid = device_sm_count();
   if (grid > units) grid = units;
   if (grid <= 0) return cudaSuccess;
-  prefill_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(qm, km, vm, p);
-  return cudaGetLastError();
+  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p);
 }
 
 }  // namespace omni

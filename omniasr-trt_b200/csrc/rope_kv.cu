@@ -11,7 +11,8 @@
 // Reference kernel this replaces: omniasr_trt/kernels.py:31-54 (_rope_kv), wrapper :294-306.
 //
 // Layout: one CTA per (token, section), section 0 = q, 1 = k, 2 = v; each thread moves 16-byte
-// vectors. The cs entries of a vector's pairs are the same D-wide row, element for element.
+// vectors. The cs entries of a vector's pairs are the same D-wide row, element for element. Launched as a
+// programmatic dependent (launch_dependent), and lets the attention after it start early the same way.
 
 #include "common.cuh"
 #include "rope_kv.cuh"
@@ -22,6 +23,8 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
   constexpr int kVec = Elem<T>::kVec;
   constexpr int kPerHead = D / kVec;
+  grid_launch_dependents();  // the attention that follows may start its set-up
+  grid_dependency_wait();    // qkv, positions and the caches may come from the kernel before
   const int64_t b = blockIdx.x;
   const int part = blockIdx.y;
   const int64_t p = a.pos[b];
@@ -78,27 +81,20 @@ static cudaError_t launch_rope_t(int dim, const RopeArgs& a, int n, cudaStream_t
   dim3 grid((unsigned)n, 3u);
   switch (dim) {
     case 16:
-      rope_kv_kernel<T, 16><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 16>, grid, dim3(256), 0, s, a);
     case 32:
-      rope_kv_kernel<T, 32><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 32>, grid, dim3(256), 0, s, a);
     case 64:
-      rope_kv_kernel<T, 64><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 64>, grid, dim3(256), 0, s, a);
     case 128:
-      rope_kv_kernel<T, 128><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 128>, grid, dim3(256), 0, s, a);
     case 256:
-      rope_kv_kernel<T, 256><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 256>, grid, dim3(256), 0, s, a);
     case 512:
-      rope_kv_kernel<T, 512><<<grid, 256, 0, s>>>(a);
-      break;
+      return launch_dependent(rope_kv_kernel<T, 512>, grid, dim3(256), 0, s, a);
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_rope_kv(int dtype, int dim, const RopeArgs& a, int n, cudaStream_t stream) {
