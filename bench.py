@@ -482,9 +482,10 @@ class Sweep(Workload):
 
     def __init__(self, device, rank, world, layers):
         super().__init__(device, rank, world, len(self.CASES))
-        if self.ROWS % world:
-            raise SystemExit(f"sweep: {self.ROWS} rows do not split over {world} ranks")
-        self.rows = self.ROWS // world
+        from omniasr_b200 import shard
+
+        a, b = shard.shard_bounds(self.ROWS, world, rank)  # this rank's contiguous shard of the 64 rows
+        self.rows = b - a
         self.keys = [L if t == 1 else keys_bucket(L + t) for t, L in self.CASES]
         cap = max(self.keys)
         self.kc = self.randn(self.rows, H, cap, D)
@@ -603,6 +604,8 @@ def cpu_time(wl, seconds: float) -> dict:
 def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
+    from omniasr_b200 import shard
+
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     wl = WORKLOADS[args.workload](device, rank, world, args.layers)
@@ -632,11 +635,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(x, device=device)
 
     # --- device-resident timing (value) ---
     for _ in range(args.warmup):
