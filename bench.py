@@ -733,6 +733,193 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
+
+# ------------------------------------------------------------------------------------- full decoder step (config 4)
+
+STEP_B, STEP_W, STEP_STEPS, STEP_SYNC = 8, 1500, 256, 8
+
+
+def reference_modules(ours: bool):
+    """The reference package (Wataru-Nakata/omniasr-trt) from baseline/_ref, with this library's kernels in place of
+    its ``omniasr_trt.kernels`` when ``ours`` (the drop-in); (modules, None) or (None, why not)."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "omniasr_trt" / "spec.py").exists():
+        return None, "the reference package is not installed in baseline/_ref"
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    if ours:
+        from omniasr_b200 import dropin
+
+        dropin.install()
+    from omniasr_trt import decode, llm, modeling, spec
+
+    return {"decode": decode, "llm": llm, "modeling": modeling, "spec": spec}, None
+
+
+def step_model(mods, device, seed: int = 0, dtype=torch.bfloat16):
+    """BASELINE config 4's decoder: 12 layers, d 4096, 32 x 128 heads, SwiGLU 11008, vocab 10288, RMSNorm; weights
+    N(0, 0.02) in bf16, norm weights 1, a 1-layer stand-in encoder (never run). The LM head's EOS row is zero, so
+    no row stops early and every step runs the full batch."""
+    modeling = mods["modeling"]
+    enc = modeling.EncoderConfig(model_dim=16, num_layers=1, num_heads=2, ffn_dim=32, feature_dim=8,
+                                 conv_layers=((8, 10, 5),), pos_kernel=4, pos_groups=2)
+    dec = modeling.DecoderConfig(model_dim=4096, num_layers=12, num_heads=32, ffn_dim=11008, vocab_size=10288)
+    with torch.device(device):
+        m = modeling.LLMModel(enc, dec)
+    m = m.to(dtype).eval()
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for name, prm in m.named_parameters():
+            if name.endswith("layer_norm.weight"):
+                prm.fill_(1.0)
+            else:
+                prm.normal_(0.0, 0.02, generator=g)
+        m.final_proj.weight[mods["llm"].EOS].zero_()
+    m.rope = modeling.rope_table(dec, device)
+    return m
+
+
+def step_bytes(m, lengths_mean: float, b: int, width: int) -> int:
+    """Unique HBM bytes of one decoder step: every decoder weight and the LM head once, plus the K/V of every key
+    the rows' last queries see (12 layers x 16,384 B per key), at the run's mean cached length."""
+    w = sum(p.numel() * p.element_size() for p in m.llama_decoder.parameters())
+    w += m.final_proj.weight.numel() * m.final_proj.weight.element_size()
+    kv = LAYERS * KV_TOKEN // 2 * m.final_proj.weight.element_size()  # K + V of one key, every layer
+    return int(w + kv * b * (lengths_mean + width))
+
+
+def decode_run(mods, dec, ctxs, steps: int, timed: bool):
+    """Prefill ``ctxs`` into slots 0..B-1 and run ``steps`` drafted decoder steps through the reference's own step
+    graphs (dec.runner), checking positions on the host every STEP_SYNC steps as its decode loop does; returns
+    (prefill ms, steps ms, first / last positions) when timed."""
+    llm, dlib = mods["llm"], mods["decode"]
+    b, dev = len(ctxs), dec.device
+    dec.done[:b] = True
+    dec.last[:b] = 0
+    dec.tok[:b] = 0
+    dec.ensure_capacity(max(max(c.size(0) for c in ctxs), dec.context_floor) + dec.reserve)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    torch.cuda.synchronize(dev)
+    ev[0].record()
+    first = dec.prefill(ctxs, list(range(b)))
+    ev[1].record()
+    idx = torch.arange(b, device=dev)
+    pos = torch.tensor([c.size(0) - 1 for c in ctxs], device=dev)
+    dec.out[idx] = llm.PAD
+    dec.out[idx, pos] = first.to(torch.int32)
+    dec.tok[idx] = first
+    dec.last[idx] = pos
+    dec.done[idx] = (first == llm.EOS) | (pos >= dlib.LIMIT)
+    dec.filled(list(range(b)), list(range(b)))
+    start_pos = pos.clone()
+    for _ in range(steps // STEP_SYNC):
+        last = dec.last[:b].cpu()
+        need = int(last.max()) + STEP_SYNC * dec.step_tokens + 2
+        if need > dec.capacity:
+            dec.ensure_capacity(need + dec.reserve)
+        keys = min(dec.capacity, -(-need // dlib.KEY_BUCKET) * dlib.KEY_BUCKET)
+        run = dec.runner(b, keys)
+        for _ in range(STEP_SYNC):
+            run()
+    ev[2].record()
+    torch.cuda.synchronize(dev)
+    return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), start_pos.cpu(), dec.last[:b].cpu()
+
+
+def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict | None:
+    """the reference's SpecDecoder (spec-4, batch 8, CUDA graphs) on a random-init decoder, with
+    this library's kernels dropped in (``ours``) or the reference's own Triton kernels."""
+    import hashlib
+
+    from omniasr_b200 import shard
+
+    impl = "b200" if ours else "reference"
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    mods, why = reference_modules(ours)
+    if mods is None:
+        return {"impl": impl, "unavailable": why} if rank == 0 else None
+    torch.manual_seed(0)
+    dtype = torch.float32 if args.dtype == "f32" else torch.bfloat16
+    m = step_model(mods, device, dtype=dtype)
+    steps = args.decode_steps
+    g = torch.Generator().manual_seed(1 + rank)
+    ctx_host = [torch.randn(STEP_W, 4096, generator=g).to(dtype).pin_memory() for _ in range(STEP_B)]
+    ctxs = [c.to(device) for c in ctx_host]
+    dec = mods["spec"].SpecDecoder(m, draft_tokens=4, max_batch=STEP_B, sync_every=STEP_SYNC, reserve=1536)
+    with torch.inference_mode():
+        decode_run(mods, dec, ctxs, steps, timed=False)  # captures every key bucket's step graph
+        for _ in range(max(0, args.warmup - 3)):
+            decode_run(mods, dec, ctxs, steps, timed=False)
+        clocks = Clocks(device.index) if rank == 0 else None
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        runs = [decode_run(mods, dec, ctxs, steps, timed=True) for _ in range(3)]
+        clock = clocks.stop() if clocks else None
+        pre_ms = float(np.median([r[0] for r in runs]))
+        steps_ms = float(np.median([r[1] for r in runs]))
+        p0, p1 = runs[-1][2], runs[-1][3]
+        tokens = dec.out[:STEP_B].cpu()
+        # end to end: contexts from pinned host memory, tokens back to the host (median of 3)
+        e2e = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(device)
+            e0.record()
+            ctx_dev = [c.to(device, non_blocking=True) for c in ctx_host]
+            decode_run(mods, dec, ctx_dev, steps, timed=True)
+            out_host = dec.out[:STEP_B].to("cpu", non_blocking=True)
+            e1.record()
+            torch.cuda.synchronize(device)
+            e2e.append(e0.elapsed_time(e1))
+        e2e_ms = float(np.median(e2e))
+    if args.tokens_out and rank == 0:
+        np.save(args.tokens_out, tokens[:, STEP_W - 1:].numpy())
+    steps_ms = shard.max_over_ranks(steps_ms, device=device)
+    pre_ms = shard.max_over_ranks(pre_ms, device=device)
+    e2e_ms = shard.max_over_ranks(e2e_ms, device=device)
+    if rank != 0:
+        return None
+    gen = (p1 - p0).tolist()
+    mean_len = float((p0.float() + p1.float()).mean() / 2)
+    nbytes = step_bytes(m, mean_len, STEP_B, dec.step_tokens)
+    pk = peaks()
+    steps_s = steps / (steps_ms * 1e-3)
+    digest = hashlib.sha256(tokens[:, STEP_W - 1:].numpy().tobytes()).hexdigest()[:16]
+    assert torch.equal(out_host[:, STEP_W - 1:], tokens[:, STEP_W - 1:]), "the decoder is not deterministic"
+    line = {
+        "metric": "decoder steps/s (spec-4, batch 8, 12 layers, CUDA graphs)", "value": round(world * steps_s, 2),
+        "unit": "steps/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3) - 2,
+        "ms_per_step": round(steps_ms / steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": args.dtype, "impl": impl,
+        "data": "synthetic: N(0,1) bf16 prefix embeddings (8 x 1500 frames), decoder weights N(0,0.02), LM-head EOS row "
+                "zeroed so every row runs all steps; no draft text (proposals from the rows' own tokens)",
+        "config": {"workload": "BASELINE config 4: the reference's SpecDecoder (draft_tokens 4, batch 8 per GPU, "
+                               "sync_every 8) on a 12-layer d4096 32x128 SwiGLU-11008 vocab-10288 decoder; prefill "
+                               "of 8 x 1500 frames, then 256 steps",
+                   "kernels": "omniasr_b200 (drop-in)" if ours else "the reference's Triton kernels",
+                   "global_batch": STEP_B * world, "prefill_ms": round(pre_ms, 3), "timing": "median of 3 runs",
+                   "prefill_frames_per_s": round(world * STEP_B * STEP_W / (pre_ms * 1e-3), 1),
+                   "tokens_generated": gen, "tokens_per_s": round(world * sum(gen) / (steps_ms * 1e-3), 1),
+                   "tokens_digest": digest, "parallelism": f"request-sharded dp{world} (no collective)"},
+        "e2e": {"value": round(world * steps / (e2e_ms * 1e-3), 2), "unit": "steps/s",
+                "ms_total": round(e2e_ms, 3),
+                "h2d_bytes_per_step": int(STEP_B * STEP_W * 4096 * ctx_host[0].element_size() / steps),
+                "d2h_bytes_per_step": int(tokens.numel() * 4 / steps),
+                "path": "contexts copied from pinned host memory, prefill + 256 steps, tokens copied back (per-step "
+                        "bytes are the totals / 256)"},
+        "roofline": {"bound": "hbm", "achieved": round(nbytes / (steps_ms / steps * 1e-3) / 1e9, 1),
+                     "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": round(nbytes / (steps_ms / steps * 1e-3) / 1e9 / pk["hbm"], 3),
+                     "peak_kind": pk["kind"], "kernel": "whole decoder step (weights + K/V read once)",
+                     "traffic": None, "bytes_per_step": nbytes},
+        "gpu_launches": 3 * LAYERS * steps if ours else 0,
+        "clocks": clock,
+    }
+    return line
+
 # --------------------------------------------------------------------------------------------------- reference arm
 
 
@@ -767,14 +954,36 @@ def main():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="verify")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["step"], default="verify")
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length (0: none)")
+    p.add_argument("--tokens-out", default=None, help="step workload: save the generated tokens (.npy)")
+    p.add_argument("--decode-steps", type=int, default=STEP_STEPS, help="step workload: decoder steps per run")
+    p.add_argument("--dtype", choices=["bf16", "f32"], default="bf16", help="step workload: model dtype")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "step":  # both arms on the GPU: this library's kernels, or the reference's own
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+        try:
+            line = run_step(args, rank, world, local_rank, ours=args.impl == "b200")
+            if line:
+                print(json.dumps(line), flush=True)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.destroy_process_group()
+        return
     if args.impl == "reference":
         line = run_reference(args, rank)
         if line:
