@@ -129,6 +129,29 @@ int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_
                            int64_t dst_row_stride, const void* parent, int parent_is_int64, int rows,
                            int64_t row_bytes, int* status, cudaStream_t stream);
 
+/* Speculative decoding's proposal for rows 0..rows-1: `tokens` proposed tokens per row (int64 `proposals`
+ * [rows, tokens]), whether they come from the draft (`use_draft`, one byte per row) and the draft position of the
+ * first (`start`). `out` holds each row's tokens by position (int32, row stride `out_stride` elements, `out_cap`
+ * positions), `draft` its draft (int32, `draft_stride`, `draft_cap`); `draft_len`, `last` (position of the newest
+ * token), `first` (position of the segment's first) and `next` (draft position expected after the newest) are
+ * int64 per row. `reach` holds 4 (distance, matching tokens needed) pairs. Bit-exact with
+ * omniasr_trt/kernels.py:361-377 (`propose`: _propose, :214-262). */
+int omniasr_propose(const int32_t* out, int64_t out_stride, int64_t out_cap, const int32_t* draft,
+                    int64_t draft_stride, int64_t draft_cap, const int64_t* draft_len, const int64_t* last,
+                    const int64_t* first, const int64_t* next, int64_t* start, int64_t* proposals,
+                    uint8_t* use_draft, int rows, int tokens, int ngram, int behind, int ahead, const int* reach,
+                    int self_window, int self_min, int* status, cudaStream_t stream);
+
+/* After a drafted step, in place on rows 0..rows-1: `tokens` [rows, width] were fed (the newest token, then the
+ * proposal) and `argmax` [rows, width] is the greedy token after each (int64). A running row (done == 0) keeps
+ * argmax 0..n at positions last+1+j of `out` (n: its leading proposed tokens equal to the argmax before them, cut
+ * at the first EOS or position >= limit among those), and advances tok, last, done and draft_next (from `start`
+ * when use_draft). Bit-exact with omniasr_trt/kernels.py:380-391 (`accept`: _accept, :264-291). */
+int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, int64_t out_stride, int64_t out_cap,
+                   int64_t* tok, int64_t* last, uint8_t* done, int64_t* draft_next, const int64_t* start,
+                   const uint8_t* use_draft, int rows, int width, int64_t limit, int64_t eos, int* status,
+                   cudaStream_t stream);
+
 /* Flash-decode for callers that cannot allocate device memory (no counterpart in the reference, whose
  * wrappers allocate their partials with torch.empty): the same computation and arguments as
  * omniasr_decode_attention() minus the workspace, which here is a device array inside this library of

@@ -11,6 +11,7 @@
 #include "omniasr_b200.h"
 #include "prefill.cuh"
 #include "rope_kv.cuh"
+#include "spec.cuh"
 
 namespace {
 
@@ -450,6 +451,85 @@ int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_
   a.row_bytes = row_bytes;
   a.status = status;
   return cuda_status(omni::launch_gather(a, rows, stream), "reorder_gather launch");
+}
+
+int omniasr_propose(const int32_t* out, int64_t out_stride, int64_t out_cap, const int32_t* draft,
+                    int64_t draft_stride, int64_t draft_cap, const int64_t* draft_len, const int64_t* last,
+                    const int64_t* first, const int64_t* next, int64_t* start, int64_t* proposals,
+                    uint8_t* use_draft, int rows, int tokens, int ngram, int behind, int ahead, const int* reach,
+                    int self_window, int self_min, int* status, cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (rows < 0 || rows > 65535) return fail(OMNIASR_ERR_ARGUMENT, "propose: rows %d", rows);
+  if (rows == 0) return ok();
+  if (!out || !draft || !draft_len || !last || !first || !next || !start || !proposals || !use_draft || !reach)
+    return fail(OMNIASR_ERR_ARGUMENT, "propose: null pointer");
+  if (tokens < 1 || ngram < 1 || ngram > omni::kProposeMaxNgram || behind < 0 || ahead < 0 || self_window < 1)
+    return fail(OMNIASR_ERR_ARGUMENT, "propose: tokens %d, ngram %d (1..%d), behind %d, ahead %d, self_window %d",
+                tokens, ngram, omni::kProposeMaxNgram, behind, ahead, self_window);
+  int self_slots = 1;
+  while (self_slots < self_window) self_slots <<= 1;  // as the reference's launch (kernels.py:372-373)
+  if (behind + ahead + 1 > omni::kProposeMaxThreads || self_slots > omni::kProposeMaxThreads ||
+      tokens > omni::kProposeMaxThreads)
+    return fail(OMNIASR_ERR_UNSUPPORTED, "propose: at most %d draft candidates, own candidates and tokens",
+                omni::kProposeMaxThreads);
+  if (out_stride < 0 || draft_stride < 0 || out_cap < 1 || draft_cap < 0)
+    return fail(OMNIASR_ERR_ARGUMENT, "propose: strides / capacities");
+  omni::ProposeArgs a{};
+  a.out = out;
+  a.s_out = out_stride;
+  a.out_cap = out_cap;
+  a.draft = draft;
+  a.s_draft = draft_stride;
+  a.draft_cap = draft_cap;
+  a.draft_len = draft_len;
+  a.last = last;
+  a.first = first;
+  a.next = next;
+  a.start = start;
+  a.prop = proposals;
+  a.use_draft = use_draft;
+  a.tokens = tokens;
+  a.ngram = ngram;
+  a.behind = behind;
+  a.ahead = ahead;
+  a.self_slots = self_slots;
+  a.self_min = self_min;
+  for (int r = 0; r < 4; ++r) {
+    a.reach_dist[r] = reach[2 * r];
+    a.reach_need[r] = reach[2 * r + 1];
+  }
+  a.status = status;
+  return cuda_status(omni::launch_propose(a, rows, stream), "propose launch");
+}
+
+int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, int64_t out_stride, int64_t out_cap,
+                   int64_t* tok, int64_t* last, uint8_t* done, int64_t* draft_next, const int64_t* start,
+                   const uint8_t* use_draft, int rows, int width, int64_t limit, int64_t eos, int* status,
+                   cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (rows < 0 || width < 1 || width > 1024) return fail(OMNIASR_ERR_ARGUMENT, "accept: rows %d, width %d", rows, width);
+  if (rows == 0) return ok();
+  if (!tokens || !argmax || !out || !tok || !last || !done || !draft_next || !start || !use_draft)
+    return fail(OMNIASR_ERR_ARGUMENT, "accept: null pointer");
+  if (out_stride < 0 || out_cap < 1) return fail(OMNIASR_ERR_ARGUMENT, "accept: out stride / capacity");
+  omni::AcceptArgs a{};
+  a.tokens = tokens;
+  a.argmax = argmax;
+  a.out = out;
+  a.s_out = out_stride;
+  a.out_cap = out_cap;
+  a.tok = tok;
+  a.last = last;
+  a.done = done;
+  a.draft_next = draft_next;
+  a.start = start;
+  a.use_draft = use_draft;
+  a.rows = rows;
+  a.width = width;
+  a.limit = limit;
+  a.eos = eos;
+  a.status = status;
+  return cuda_status(omni::launch_accept(a, stream), "accept launch");
 }
 
 }  // extern "C"

@@ -2,11 +2,12 @@
 
 After :func:`install`, ``import omniasr_trt.kernels`` (and the ``from . import kernels`` of ``decode``, ``spec``,
 ``beam`` and ``llm``) yields a module whose path functions -- ``available``, ``rope_kv``, ``decode_attention``,
-``draft_attention``, ``beam_attention``, ``splits_for``, ``ATTN``, ``DRAFT_ATTN`` -- are this package's CUDA
-kernels, and the prefill's causal ``F.scaled_dot_product_attention`` in ``decode.py`` (decode.py:171) runs
-:func:`omniasr_b200.kernels.prefill_attention`. The speculative decoder's control kernels ``propose`` / ``accept``
-are not on this path and stay the reference's own. Nothing else of the reference changes: its decoders,
-CUDA-graph capture, ``OmniASRLLM.transcribe`` and ``compat.Pipeline`` run unchanged on top.
+``draft_attention``, ``beam_attention``, ``splits_for``, ``ATTN``, ``DRAFT_ATTN`` and the speculative decoder's
+control kernels ``propose`` / ``accept`` -- are this package's CUDA kernels, and the prefill's causal
+``F.scaled_dot_product_attention`` in ``decode.py`` (decode.py:171) runs
+:func:`omniasr_b200.kernels.prefill_attention`. No Triton kernel of the reference remains on these decoders' path.
+Nothing else of the reference changes: its decoders, CUDA-graph capture, ``OmniASRLLM.transcribe`` and
+``compat.Pipeline`` run unchanged on top.
 """
 
 from __future__ import annotations
@@ -16,7 +17,7 @@ import sys
 import types
 
 PATH_FUNCTIONS = ("available", "rope_kv", "decode_attention", "draft_attention", "beam_attention", "splits_for",
-                  "ATTN", "DRAFT_ATTN")
+                  "ATTN", "DRAFT_ATTN", "propose", "accept")
 
 
 class _Functional(types.ModuleType):

@@ -242,6 +242,63 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
     return o.view(b, width, heads, dim).transpose(1, 2)
 
 
+def _vec(t: torch.Tensor, dtype: torch.dtype, name: str) -> torch.Tensor:
+    if t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor")
+    return t
+
+
+def propose(out: torch.Tensor, draft: torch.Tensor, draft_len: torch.Tensor, last: torch.Tensor,
+            first: torch.Tensor, nxt: torch.Tensor, start: torch.Tensor, tokens: int, ngram: int, behind: int,
+            ahead: int, reach: tuple, self_window: int, self_min: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Drafted decoding's proposals of rows 0..B-1 (B = ``last.numel()``): ``tokens`` ids each [B, k] (int64) and
+    whether they come from the draft [B] (bool); ``start`` [B] (int64) gets the draft position of the first one.
+    ``out`` [>=B, S] / ``draft`` [>=B, C] int32 token rows (unit inner stride); ``draft_len``, ``last``, ``first``,
+    ``nxt`` int64 [B]; ``reach`` 4 (distance, matching tokens) pairs. Bit-exact with the reference's ``propose``
+    (kernels.py:361-377)."""
+    b = last.numel()
+    prop = torch.empty(b, tokens, device=out.device, dtype=torch.long)
+    use_draft = torch.empty(b, device=out.device, dtype=torch.bool)
+    if b == 0:
+        return prop, use_draft
+    if out.dtype != torch.int32 or draft.dtype != torch.int32 or out.stride(1) != 1 or draft.stride(1) != 1:
+        raise ValueError("propose: out and draft must be int32 with unit inner stride")
+    for t, name in ((draft_len, "draft_len"), (last, "last"), (first, "first"), (nxt, "nxt"), (start, "start")):
+        _vec(t, torch.int64, name)
+    pairs = [int(x) for pair in reach for x in pair]
+    if len(pairs) != 8:
+        raise ValueError("propose: reach must hold 4 (distance, tokens) pairs")
+    creach = (ctypes.c_int * 8)(*pairs)
+    _lib.call("omniasr_propose", _ptr(out), out.stride(0), out.size(1), _ptr(draft), draft.stride(0), draft.size(1),
+              _ptr(draft_len), _ptr(last), _ptr(first), _ptr(nxt), _ptr(start), _ptr(prop), _ptr(use_draft), b,
+              int(tokens), int(ngram), int(behind), int(ahead), ctypes.cast(creach, ctypes.c_void_p),
+              int(self_window), int(self_min), _ptr(status_word(out.device)), _stream(out.device))
+    return prop, use_draft
+
+
+def accept(tokens: torch.Tensor, nxt: torch.Tensor, out: torch.Tensor, tok: torch.Tensor, last: torch.Tensor,
+           done: torch.Tensor, draft_next: torch.Tensor, start: torch.Tensor, use_draft: torch.Tensor, limit: int,
+           eos: int) -> None:
+    """In place on rows 0..B-1 after a drafted step: ``tokens`` fed [B, T] (the newest token, then the proposal) and
+    ``nxt`` the argmax after each [B, T] (int64); ``out`` [>=B, S] int32; ``tok`` / ``last`` / ``draft_next`` /
+    ``start`` [B] int64, ``done`` / ``use_draft`` [B] bool. Bit-exact with the reference's ``accept``
+    (kernels.py:380-391)."""
+    b, width = tokens.shape
+    if b == 0:
+        return
+    _vec(tokens, torch.int64, "tokens")
+    _vec(nxt, torch.int64, "nxt")
+    for t, name in ((tok, "tok"), (last, "last"), (draft_next, "draft_next"), (start, "start")):
+        _vec(t, torch.int64, name)
+    _vec(done, torch.bool, "done")
+    _vec(use_draft, torch.bool, "use_draft")
+    if out.dtype != torch.int32 or out.stride(1) != 1:
+        raise ValueError("accept: out must be int32 with unit inner stride")
+    _lib.call("omniasr_accept", _ptr(tokens), _ptr(nxt), _ptr(out), out.stride(0), out.size(1), _ptr(tok),
+              _ptr(last), _ptr(done), _ptr(draft_next), _ptr(start), _ptr(use_draft), b, width, int(limit),
+              int(eos), _ptr(status_word(out.device)), _stream(out.device))
+
+
 def reorder_gather(src: torch.Tensor, parent: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``out[r] = src[parent[r]]`` along dim 0, byte-exact (``torch.index_select(src, 0, parent)``); each row of
     ``src`` / ``out`` must be contiguous. ``out`` (optional) must not overlap ``src``."""

@@ -13,7 +13,10 @@ those files, so they run where the reference is absent. Which reference code pro
 * ``decode_*.npz``   -- ``F.scaled_dot_product_attention`` per row, the reference-order q_len-1 attention
                         (modeling.py:396-397), float64; rows of length 0 are zeros (kernels.py:8-9);
 * ``draft_*.npz``    -- the ``tril(past)`` mask + SDPA of ``LLMModel.decoder_forward`` (modeling.py:400-403), float64;
-* ``beam_*.npz``     -- ``BeamDecoder.attention`` on its PyTorch branch (beam.py:215-233), float64 model.
+* ``beam_*.npz``     -- ``BeamDecoder.attention`` on its PyTorch branch (beam.py:215-233), float64 model;
+* ``propose.npz``    -- ``reference_propose``, the PyTorch statement of the speculative proposal that the
+                        reference's own kernel test checks its Triton kernel against (tests/test_spec.py:43-92,
+                        :206-228), on inputs drawn like that test's (few symbols: many partial matches and ties).
 """
 
 from __future__ import annotations
@@ -156,6 +159,47 @@ def beam_case(is_bf16: bool):
                         digest=gi.digest(q, kc, vc, ctx_len, kg, vg, ptr, gen_len))
 
 
+def propose_case(ref_src: str):
+    """Twelve trials of 8 rows (proposal lengths 1, 4 and 7), the reference's constants (spec.py:33-39)."""
+    from types import SimpleNamespace
+
+    tests_dir = str(Path(ref_src).resolve().parent / "tests")
+    if tests_dir not in sys.path:
+        sys.path.insert(0, tests_dir)
+    import test_spec as ts  # the reference's test module: its reference_propose
+    from omniasr_trt import spec
+
+    rng = np.random.default_rng(40)
+    b, cap, dcap = 8, 2048, spec.DRAFT_CAPACITY
+    fields = {k: [] for k in ("k", "out", "draft", "draft_len", "last", "first", "nxt", "prop", "use_draft", "start")}
+    for trial in range(12):
+        k = (1, 4, 7)[trial % 3]
+        vocab = 4 + trial % 5
+        out = rng.integers(3, vocab, (b, cap)).astype(np.int32)
+        first = rng.integers(0, 600, b)
+        last = first + rng.integers(0, 1400, b)
+        last[0] = first[0]
+        out[np.arange(cap)[None, :] < first[:, None]] = 1  # PAD before the segment
+        draft = rng.integers(3, vocab, (b, dcap)).astype(np.int32)
+        dlen = rng.integers(0, dcap + 1, b)
+        dlen[1] = 0
+        draft[np.arange(dcap)[None, :] >= dlen[:, None]] = -1
+        nxt = (rng.random(b) * (dlen + 8)).astype(np.int64)
+        st = SimpleNamespace(device=torch.device("cpu"), draft_tokens=k, out=torch.from_numpy(out),
+                             draft=torch.from_numpy(draft), draft_len=torch.from_numpy(dlen),
+                             last=torch.from_numpy(last), first=torch.from_numpy(first), next=torch.from_numpy(nxt))
+        prop, use_draft, start = ts.reference_propose(st, b)
+        pad = np.zeros((b, 7), dtype=np.int64)
+        pad[:, :k] = prop.numpy()
+        for name, v in (("k", k), ("out", out), ("draft", draft), ("draft_len", dlen), ("last", last),
+                        ("first", first), ("nxt", nxt), ("prop", pad), ("use_draft", use_draft.numpy()),
+                        ("start", start.numpy())):
+            fields[name].append(v)
+    consts = dict(ngram=spec.NGRAM, behind=spec.BEHIND, ahead=spec.AHEAD, reach=np.array(spec.REACH),
+                  self_window=spec.SELF_WINDOW, self_min=spec.SELF_MIN)
+    np.savez_compressed(HERE / "propose.npz", **{k: np.stack(v) for k, v in fields.items()}, **consts)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--reference", default="/root/reference/src", help="the reference's src/ directory")
@@ -171,6 +215,7 @@ def main():
         decode_case(is_bf16)
         draft_case(is_bf16)
         beam_case(is_bf16)
+    propose_case(args.reference)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

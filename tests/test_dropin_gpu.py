@@ -34,6 +34,7 @@ def ref():
 
     assert decode.kernels is k and spec.kernels is k and beam.kernels is k
     assert k.rope_kv is ours.rope_kv and k.decode_attention is ours.decode_attention
+    assert k.propose is ours.propose and k.accept is ours.accept  # no reference Triton kernel left on the path
     assert isinstance(decode.F, dropin._Functional)  # the prefill's causal SDPA runs prefill_attention
     return {"decode": decode, "spec": spec, "beam": beam, "llm": llm, "modeling": modeling, "kernels": k}
 

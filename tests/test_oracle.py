@@ -5,6 +5,7 @@ import pytest
 import torch
 
 import inputs as gi
+from conftest import GOLDEN
 from oracle import attention, bf16, gather, rope, splits
 
 
@@ -98,3 +99,49 @@ def test_oracle_catches_a_planted_error(golden):
     wrong = attention.decode_attention(_t(q, False), _t(k, False), _t(v, False), torch.from_numpy(lengths) + 1,
                                        float(g["scale"]))
     assert np.abs(wrong.numpy() - g["out"]).max() > 1e-3
+
+
+def test_propose_oracle_matches_reference_golden():
+    """The speculative proposal (oracle.spec.propose) against the reference's own PyTorch statement of it
+    (tests/test_spec.py:43-92 of the reference), twelve trials of 8 rows with few symbols."""
+    from oracle import spec as ospec
+
+    d = np.load(GOLDEN / "propose.npz")
+    reach = [tuple(int(x) for x in r) for r in d["reach"]]
+    for t in range(len(d["k"])):
+        k = int(d["k"][t])
+        prop, use_draft, start = ospec.propose(d["out"][t], d["draft"][t], d["draft_len"][t], d["last"][t],
+                                               d["first"][t], d["nxt"][t], k, int(d["ngram"]), int(d["behind"]),
+                                               int(d["ahead"]), reach, int(d["self_window"]), int(d["self_min"]))
+        assert np.array_equal(use_draft, d["use_draft"][t]), t
+        assert np.array_equal(start, d["start"][t]), t
+        assert np.array_equal(prop, d["prop"][t][:, :k]), t
+
+
+def test_accept_oracle_rules():
+    """oracle.spec.accept on hand-made rows: leading matches kept, EOS and the length limit end a row inside the
+    step, finished rows untouched (the reference's _accept, kernels.py:264-291)."""
+    from oracle import spec as ospec
+
+    eos, limit = 2, 100
+    tokens = np.array([[7, 5, 6, 9], [7, 5, 6, 9], [7, 5, 6, 9], [7, 5, 6, 9], [7, 5, 6, 9]], dtype=np.int64)
+    nxt = np.array([[5, 6, 8, 4], [5, 2, 9, 4], [3, 6, 9, 4], [5, 6, 9, 4], [5, 6, 9, 4]], dtype=np.int64)
+    out = np.full((5, 128), 1, dtype=np.int32)
+    tok = np.zeros(5, dtype=np.int64)
+    last = np.array([10, 10, 10, 97, 10], dtype=np.int64)
+    done = np.array([False, False, False, False, True])
+    draft_next = np.array([20, 20, 20, 20, 20], dtype=np.int64)
+    start = np.array([30, 30, 30, 30, 30], dtype=np.int64)
+    use_draft = np.array([True, False, True, True, True])
+    ospec.accept(tokens, nxt, out, tok, last, done, draft_next, start, use_draft, limit, eos)
+    # row 0: 5, 6 match the fed tokens, 8 does not -> argmax 0..2 kept
+    assert list(out[0, 11:14]) == [5, 6, 8] and last[0] == 13 and tok[0] == 8 and not done[0]
+    assert draft_next[0] == 30 + 3
+    # row 1: EOS at argmax 1 (within the kept run) ends the row there
+    assert list(out[1, 11:13]) == [5, 2] and last[1] == 12 and tok[1] == 2 and done[1] and draft_next[1] == 22
+    # row 2: first argmax differs from the fed token: one token
+    assert out[2, 11] == 3 and out[2, 12] == 1 and last[2] == 11 and draft_next[2] == 31
+    # row 3: positions 98, 99 kept, 100 reaches the limit and ends the row
+    assert list(out[3, 98:101]) == [5, 6, 9] and last[3] == 100 and done[3]
+    # row 4: finished, untouched
+    assert last[4] == 10 and (out[4] == 1).all() and draft_next[4] == 20
