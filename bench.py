@@ -899,7 +899,8 @@ def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict |
         "config": {"workload": "BASELINE config 4: the reference's SpecDecoder (draft_tokens 4, batch 8 per GPU, "
                                "sync_every 8) on a 12-layer d4096 32x128 SwiGLU-11008 vocab-10288 decoder; prefill "
                                "of 8 x 1500 frames, then 256 steps",
-                   "kernels": "omniasr_b200 (drop-in)" if ours else "the reference's Triton kernels",
+                   "kernels": "omniasr_b200 (drop-in: attention, RoPE/append, prefill, propose, accept)" if ours
+                   else "the reference's Triton kernels",
                    "global_batch": STEP_B * world, "prefill_ms": round(pre_ms, 3), "timing": "median of 3 runs",
                    "prefill_frames_per_s": round(world * STEP_B * STEP_W / (pre_ms * 1e-3), 1),
                    "tokens_generated": gen, "tokens_per_s": round(world * sum(gen) / (steps_ms * 1e-3), 1),
@@ -915,7 +916,7 @@ def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict |
                      "frac": round(nbytes / (steps_ms / steps * 1e-3) / 1e9 / pk["hbm"], 3),
                      "peak_kind": pk["kind"], "kernel": "whole decoder step (weights + K/V read once)",
                      "traffic": None, "bytes_per_step": nbytes},
-        "gpu_launches": 3 * LAYERS * steps if ours else 0,
+        "gpu_launches": (3 * LAYERS + 2) * steps if ours else 0,  # rope_kv, pass, combine per layer; propose, accept
         "clocks": clock,
     }
     return line

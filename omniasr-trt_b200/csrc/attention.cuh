@@ -54,6 +54,10 @@ void carve_partials(void* ws, int64_t rows_q, int heads, int st, int dim, float*
 
 cudaError_t launch_split(int dtype, int dim, bool gather, const SplitPlan& plan, const SplitArgs& a, int groups,
                          cudaStream_t stream);
+// Generated-key pass of beam attention for the tensor-core path (bf16, head_dim 128), one partial per
+// (row, head) at split a.sp_offset of a.st (beam_gen.cu).
+cudaError_t launch_gen_gather(const SplitArgs& a, int rows, cudaStream_t stream);
+
 cudaError_t launch_combine(int dtype, int dim, const float* part_o, const float* part_ml, void* out,
                            int64_t rows_heads, int st, cudaStream_t stream);
 

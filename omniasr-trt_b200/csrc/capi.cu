@@ -327,18 +327,17 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
     t.status = status;
     omni::carve_partials(workspace, rows, heads, stc, dim, &t.part_o, &t.part_ml);
     float *go, *gml;
-    omni::carve_partials(static_cast<char*>(workspace) + need_c, rows, heads, pg.splits, dim, &go, &gml);
+    omni::carve_partials(static_cast<char*>(workspace) + need_c, rows, heads, 1, dim, &go, &gml);
     if (int e = cuda_status(omni::launch_tc_pass(kc, vc, ctx_rows, ctx_len_cap, ctx_stride_row, ctx_stride_head,
                                                  ctx_stride_pos, ctx_keys, t, stream),
                             "context attention launch"))
       return e;
     b.part_o = go;
     b.part_ml = gml;
-    b.st = pg.splits;
+    b.st = 1;  // one partial per (row, head): a warp covers all of a row's generated keys
     b.sp_offset = 0;
-    if (int e = cuda_status(omni::launch_split(dtype, dim, true, pg, b, (int)rows, stream), "generated split launch"))
-      return e;
-    return cuda_status(omni::launch_tc_combine(t, out, go, gml, pg.splits, stream), "combine launch");
+    if (int e = cuda_status(omni::launch_gen_gather(b, (int)rows, stream), "generated-key launch")) return e;
+    return cuda_status(omni::launch_tc_combine(t, out, go, gml, 1, stream), "combine launch");
   }
   const omni::SplitPlan pc = omni::plan_split(dtype, dim, groups, heads, beams, ctx_keys);
   const int st = pc.splits + pg.splits;
