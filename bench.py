@@ -537,7 +537,77 @@ class Sweep(Workload):
         return one, "8 rows, q_len 5, 2048 keys (one case of the sweep): model-dtype masked softmax (torch CPU)"
 
 
-WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep)}
+class Gemm(Workload):
+    """The decoder step's four weight GEMMs for 40 token rows (BASELINE config 4's batch 8 x spec-4 + 1), 12 layers:
+    QKV, the output projection + residual, gate/inner + SwiGLU, the FFN output + residual (kernels.decode_gemm)."""
+
+    name = "gemm"
+    metric = "decode GEMM weight-streaming GB/s (QKV, out+res, SwiGLU, FFN-out+res; 40 tokens; 12 layers)"
+    roof_kernel = "decode_gemm (QKV: 12288 x 4096)"
+    traffic_key = "decode_gemm_qkv_bytes_per_call"
+    M, D_MODEL, FFN = 40, 4096, 11008
+    calls_per_layer = 4
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        M, Dm, Fn = self.M, self.D_MODEL, self.FFN
+        w = lambda r, c: (torch.randn(r, c, generator=self.gen, device=self.device) * 0.02).to(torch.bfloat16)  # noqa
+        self.w = [(w(3 * Dm, Dm), w(Dm, Dm), w(2 * Fn, Dm), w(Dm, Fn)) for _ in range(self.layers)]
+        self.x = self.randn(M, Dm)
+        self.o = self.randn(M, Dm)
+        self.h = self.randn(M, Dm)
+        self.g = self.randn(M, Fn)
+        per_layer = 2 * (3 * Dm * Dm + Dm * Dm + 2 * Fn * Dm + Dm * Fn)
+        self.roof_units = 2 * 3 * Dm * Dm
+        self.step_units = per_layer * self.layers
+        self.h2d = [self.x]
+
+    def run(self, ev=None):
+        outs = []
+        for i in range(self.layers):
+            qkv_w, out_w, gi_w, ffo_w = self.w[i]
+            if ev:
+                ev[i][0].record()
+            outs.append(self.K.decode_gemm(self.x, qkv_w))
+            if ev:
+                ev[i][1].record()
+            outs.append(self.K.decode_gemm(self.o, out_w, "residual", residual=self.h))
+            outs.append(self.K.decode_gemm(self.x, gi_w, "swiglu"))
+            outs.append(self.K.decode_gemm(self.g, ffo_w, "residual", residual=self.h))
+        self.d2h = outs[-1:]
+        return outs
+
+    def run_library(self):
+        """The same GEMMs as the reference computes them (torch / cuBLAS)."""
+        outs = []
+        for i in range(self.layers):
+            qkv_w, out_w, gi_w, ffo_w = self.w[i]
+            outs.append(self.x @ qkv_w.t())
+            outs.append(torch.addmm(self.h, self.o, out_w.t()))
+            gate, inner = (self.x @ gi_w.t()).chunk(2, -1)
+            outs.append(inner * torch.nn.functional.silu(gate))
+            outs.append(torch.addmm(self.h, self.g, ffo_w.t()))
+        return outs
+
+    def config(self):
+        return {"workload": "the decoder step's weight GEMMs (BASELINE config 4 model), 40 token rows, 12 layers of "
+                            "distinct weights (~4.8 GB per step, far above L2)",
+                "rows": self.M, "layers": self.layers, "bytes_per_step_per_gpu": self.step_units}
+
+    @classmethod
+    def cpu_sampler(cls):
+        g = cpu_gen(0)
+        x = torch.randn(cls.M, cls.D_MODEL, generator=g).to(torch.bfloat16)
+        w = (torch.randn(cls.D_MODEL, cls.D_MODEL, generator=g) * 0.02).to(torch.bfloat16)
+
+        def one():
+            x @ w.t()
+            return 2 * cls.D_MODEL * cls.D_MODEL
+
+        return one, "the output projection (4096 x 4096, 40 rows) in torch on the CPU"
+
+
+WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm)}
 
 
 # --------------------------------------------------------------------------------------------------------- timing
@@ -728,6 +798,27 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                          for (t, L), b, c in zip(wl.CASES, wl.case_bytes, case_ms)}
     if args.layers != LAYERS and args.workload not in ("sweep", "gather"):
         line["config"]["reduced"] = f"{args.layers} of {LAYERS} layers (profiling case, not a headline number)"
+    if hasattr(wl, "run_library"):  # the same work through torch / cuBLAS, graph-timed the same way
+        lib_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            wl.run_library()
+            torch.cuda.synchronize(device)
+            lib_graph.capture_begin()
+            wl.run_library()
+            lib_graph.capture_end()
+        torch.cuda.synchronize(device)
+        for _ in range(args.warmup):
+            lib_graph.replay()
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for _ in range(args.steps):
+            lib_graph.replay()
+        e3.record()
+        torch.cuda.synchronize(device)
+        lib_ms = s3.elapsed_time(e3) / args.steps
+        line["library_baseline"] = {"value": round(wl.step_units / (lib_ms * 1e-3) / scale, 1), "unit": wl.unit,
+                                    "ms_per_step": round(lib_ms, 4), "what": "torch.matmul / addmm (cuBLAS) and "
+                                    "the SwiGLU elementwise, as the reference's decoder step computes them"}
     if world == 1 and args.cpu_seconds > 0:
         line["cpu_baseline"] = cpu_time(WORKLOADS[args.workload], args.cpu_seconds)
     return line

@@ -152,6 +152,25 @@ int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, i
                    const uint8_t* use_draft, int rows, int width, int64_t limit, int64_t eos, int* status,
                    cudaStream_t stream);
 
+/* Decode-time weight GEMM for the step's few token rows (rows <= 64), bf16 in and out, fp32 accumulate:
+ *   OMNIASR_GEMM_STORE     y[m, j] = x[m, :] . w[j, :]                           (n rows of w)
+ *   OMNIASR_GEMM_RESIDUAL  y[m, j] = residual[m, j] + x[m, :] . w[j, :]          (torch.addmm(residual, x, w.t()))
+ *   OMNIASR_GEMM_SWIGLU    w = [gate; inner] (2n rows): y[m, j] = inner * silu(gate), each rounded to bf16 first
+ * x [rows, k] and w row-major with element row strides (16-byte aligned rows); y / residual [rows, n]. The
+ * workspace (omniasr_decode_gemm_workspace() bytes, 16-byte aligned) starts with per-tile arrival counters that
+ * must be ZERO when a call starts; every call that completes leaves them zero again, so a caller zeroes a
+ * workspace once and keeps it (one per stream: calls sharing a workspace must not overlap on the GPU). Replaces the decoder step's weight GEMMs
+ * of omniasr_trt/decode.py:201-205 / spec.py:100-107 (`qkv = norm(h) @ qkv_w.t()`, `torch.addmm(h, o, out_w.t())`,
+ * `(norm(h) @ gi_w.t()).chunk(2)` + `inner * F.silu(gate)`, `torch.addmm(h, ..., ffo_w.t())`), which the reference
+ * leaves to cuBLAS. */
+#define OMNIASR_GEMM_STORE 0
+#define OMNIASR_GEMM_RESIDUAL 1
+#define OMNIASR_GEMM_SWIGLU 2
+size_t omniasr_decode_gemm_workspace(int rows, int n, int k, int mode);
+int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int n, int k,
+                        int mode, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
+                        void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
+
 /* Flash-decode for callers that cannot allocate device memory (no counterpart in the reference, whose
  * wrappers allocate their partials with torch.empty): the same computation and arguments as
  * omniasr_decode_attention() minus the workspace, which here is a device array inside this library of

@@ -12,6 +12,7 @@
 #include "prefill.cuh"
 #include "rope_kv.cuh"
 #include "spec.cuh"
+#include "wgemm.cuh"
 
 namespace {
 
@@ -529,6 +530,47 @@ int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, i
   a.eos = eos;
   a.status = status;
   return cuda_status(omni::launch_accept(a, stream), "accept launch");
+}
+
+size_t omniasr_decode_gemm_workspace(int rows, int n, int k, int mode) {
+  if (rows < 1 || rows > omni::kGemmMaxRows) return 0;
+  return omni::gemm_workspace_bytes(rows, n, k, mode);
+}
+
+int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int n, int k,
+                        int mode, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
+                        void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (rows < 0 || rows > omni::kGemmMaxRows || n < 0 || k < 0)
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: rows %d (at most %d), n %d, k %d", rows, omni::kGemmMaxRows, n, k);
+  if (rows == 0 || n == 0) return ok();
+  if (k == 0) return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: k = 0");
+  if (mode != omni::kGemmStore && mode != omni::kGemmResidual && mode != omni::kGemmSwiglu)
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: mode %d", mode);
+  if (!x || !w || !y || !workspace) return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: null pointer");
+  if (mode == omni::kGemmResidual && !residual) return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: no residual");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(workspace) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+      x_stride < k || w_stride < k)
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: x / w must be 16-byte aligned with row strides >= k keeping it");
+  if (y_stride < n || (mode == omni::kGemmResidual && residual_stride < n))
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm: output / residual row stride < n");
+  if (omni::gemm_tiles(n, mode) > omni::kGemmMaxTiles)
+    return fail(OMNIASR_ERR_UNSUPPORTED, "decode_gemm: n %d needs more than %d weight tiles", n, omni::kGemmMaxTiles);
+  const size_t need = omni::gemm_workspace_bytes(rows, n, k, mode);
+  if (workspace_bytes < need)
+    return fail(OMNIASR_ERR_WORKSPACE, "decode_gemm: workspace %zu bytes, %zu needed", workspace_bytes, need);
+  omni::GemmArgs a{};
+  a.rows = rows;
+  a.n = n;
+  a.k = k;
+  a.mode = mode;
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.ld_res = residual_stride;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ld_y = y_stride;
+  a.status = status;
+  return cuda_status(omni::launch_decode_gemm(x, x_stride, w, w_stride, a, workspace, workspace_bytes, stream),
+                     "decode_gemm launch");
 }
 
 }  // extern "C"

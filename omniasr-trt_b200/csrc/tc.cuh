@@ -26,6 +26,15 @@ OMNI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int
       : "memory");
 }
 
+// 2-D tiled load into this CTA's shared memory (no multicast), completion on `bar`.
+OMNI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // 3-D tiled load into this CTA's shared memory (no multicast), completion on `bar`.
 OMNI_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
   asm volatile(

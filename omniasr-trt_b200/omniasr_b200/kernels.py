@@ -299,6 +299,51 @@ def accept(tokens: torch.Tensor, nxt: torch.Tensor, out: torch.Tensor, tok: torc
               int(eos), _ptr(status_word(out.device)), _stream(out.device))
 
 
+GEMM_MODES = {"store": 0, "residual": 1, "swiglu": 2}
+_GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters zero
+_GEMM_WS_RETIRED: list = []  # outgrown workspaces, kept alive for CUDA graphs that captured them
+
+
+def _gemm_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _GEMM_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _GEMM_WS_RETIRED.append(ws)
+        with torch.inference_mode(False):
+            ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+        _GEMM_WS[key] = ws
+    return ws
+
+
+def decode_gemm(x: torch.Tensor, w: torch.Tensor, mode: str = "store", residual: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """The decoder step's weight GEMMs for at most 64 token rows (bf16): ``x @ w.t()`` ("store"),
+    ``torch.addmm(residual, x, w.t())`` ("residual"), or with ``w`` the concatenated [gate; inner] weights
+    ``inner * F.silu(gate)`` of ``(x @ w.t()).chunk(2, -1)`` ("swiglu", each half rounded to bf16 first, as the
+    reference computes it). Rows of x and w must be contiguous with 16-byte aligned strides."""
+    rows, k = x.shape
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("decode_gemm: bf16 x and w")
+    if x.stride(1) != 1 or w.stride(1) != 1 or w.size(1) != k:
+        raise ValueError("decode_gemm: x [rows, k] and w [n, k] with unit inner stride")
+    m = GEMM_MODES[mode]
+    n = w.size(0) // 2 if mode == "swiglu" else w.size(0)
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
+    if rows == 0 or n == 0:
+        return out
+    if mode == "residual":
+        if residual is None or residual.shape != (rows, n) or residual.stride(1) != 1:
+            raise ValueError("decode_gemm: residual [rows, n] with unit inner stride")
+    lib = _lib.load()
+    ws = _gemm_workspace(lib.omniasr_decode_gemm_workspace(rows, n, k, m), x.device)
+    _lib.call("omniasr_decode_gemm", _ptr(x), x.stride(0), rows, _ptr(w), w.stride(0), n, k, m,
+              _ptr(residual) if residual is not None else None, residual.stride(0) if residual is not None else 0,
+              _ptr(out), out.stride(0), _ptr(ws), ws.numel(), _ptr(status_word(x.device)), _stream(x.device))
+    return out
+
+
 def reorder_gather(src: torch.Tensor, parent: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``out[r] = src[parent[r]]`` along dim 0, byte-exact (``torch.index_select(src, 0, parent)``); each row of
     ``src`` / ``out`` must be contiguous. ``out`` (optional) must not overlap ``src``."""
