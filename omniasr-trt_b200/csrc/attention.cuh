@@ -54,10 +54,6 @@ void carve_partials(void* ws, int64_t rows_q, int heads, int st, int dim, float*
 
 cudaError_t launch_split(int dtype, int dim, bool gather, const SplitPlan& plan, const SplitArgs& a, int groups,
                          cudaStream_t stream);
-// Generated-key pass of beam attention for the tensor-core path (bf16, head_dim 128), one partial per
-// (row, head) at split a.sp_offset of a.st (beam_gen.cu).
-cudaError_t launch_gen_gather(const SplitArgs& a, int rows, cudaStream_t stream);
-
 cudaError_t launch_combine(int dtype, int dim, const float* part_o, const float* part_ml, void* out,
                            int64_t rows_heads, int st, cudaStream_t stream);
 
@@ -83,9 +79,20 @@ bool tc_path_enabled(int dtype, int dim, int nq);
 int tc_segments(int64_t keys);
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream);
-// Merges the pass's segments (plus, for beam search, `extra_st` splits of a second partial region) into out.
-cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o, const float* extra_ml, int extra_st,
-                              cudaStream_t stream);
+// Beam search's generated keys, attended inside the combine (before it waits for the pass): row r's key j < gen_len[r]
+// comes from cache row ptr[r, j] at position j (bf16, head_dim 128).
+struct GenKeys {
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t s_kb, s_kh, s_ks, cache_rows, cache_len;  // strides in elements
+  const int32_t* ptr;
+  int64_t ptr_stride;
+  const int64_t* gen_len;  // [rows]
+  int enabled;
+};
+
+// Merges the pass's segments (and, for beam search, the generated keys' attention) into out.
+cudaError_t launch_tc_combine(const TcParams& p, void* out, const GenKeys& gen, cudaStream_t stream);
 
 bool dim_supported(int dtype, int dim);
 int device_sm_count();

@@ -685,18 +685,85 @@ __global__ void __launch_bounds__(THREADS, 1)
   OMNI_TRACE_CTA(1);
 }
 
-// Merges the segments of each (query row, head): out = sum w_s o_s / sum w_s l_s, plus (beam search) the splits
-// of a second partial region. A unit the pass finished inside one CTA was written by the pass itself.
+// Merges the segments of each (query row, head): out = sum w_s o_s / sum w_s l_s. For beam search it first attends
+// the row's generated keys itself (they do not depend on the pass, so this overlaps the pass's tail): warp w scores 8
+// of each 32 keys (lane l holds dims 4l..4l+3; all 8 loads in flight, then butterfly sums), and thread d accumulates
+// dim d over the chunk's V rows; the result is one more segment. A unit the pass finished inside one CTA was written
+// by the pass itself.
 __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int grid, __nv_bfloat16* __restrict__ out,
-                                                         const float* __restrict__ extra_o,
-                                                         const float* __restrict__ extra_ml, int extra_st) {
+                                                         const GenKeys gen) {
   __shared__ long long red_total[4], red_pre[4];
   __shared__ long long unit_tiles;
+  __shared__ float qs[D];
+  __shared__ float sc[32];
+  __shared__ long long koff[32];
   const int64_t rh = blockIdx.x;
   const int row = (int)(rh / p.heads);
   const int h = (int)(rh % p.heads);
   const int g = row / p.nq;
   const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
+
+  float gm = -INFINITY, gl = 0.f, go = 0.f;  // the generated keys' segment
+  if (gen.enabled) {
+    qs[t] = __bfloat162float(p.q[rh * D + t]);
+    int64_t n = gen.gen_len[row];
+    n = n < 0 ? 0 : (n > gen.cache_len ? gen.cache_len : n);
+    __syncthreads();
+    for (int64_t j0 = 0; j0 < n; j0 += 32) {
+      uint2 kv[8];
+      long long off[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t j = j0 + 8 * warp + i;
+        int64_t src = row;
+        if (j < n) {
+          const int64_t pj = gen.ptr[(int64_t)row * gen.ptr_stride + j];
+          if (pj < 0 || pj >= gen.cache_rows) {
+            if (lane == 0) raise_status(p.status, kStatusIndex);
+          } else {
+            src = pj;
+          }
+        }
+        off[i] = src * gen.s_kb + (int64_t)h * gen.s_kh + j * gen.s_ks;
+        kv[i] = j < n ? *reinterpret_cast<const uint2*>(gen.k + off[i] + 4 * lane) : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float d = __uint_as_float(kv[i].x << 16) * qs[4 * lane] +
+                  __uint_as_float(kv[i].x & 0xffff0000u) * qs[4 * lane + 1] +
+                  __uint_as_float(kv[i].y << 16) * qs[4 * lane + 2] +
+                  __uint_as_float(kv[i].y & 0xffff0000u) * qs[4 * lane + 3];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) {
+          const int64_t j = j0 + 8 * warp + i;
+          sc[8 * warp + i] = j < n ? d * p.qscale : -INFINITY;
+          koff[8 * warp + i] = off[i];
+        }
+      }
+      __syncthreads();
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) cm = fmaxf(cm, sc[i]);
+      const float mnew = fmaxf(gm, cm);
+      const float scale = ex2(gm - mnew);  // 0 for the first chunk
+      go *= scale;
+      gl *= scale;
+      __nv_bfloat16 vv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) vv[i] = j0 + i < n ? gen.v[koff[i] + t] : __float2bfloat16_rn(0.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float pi = j0 + i < n ? ex2(sc[i] - mnew) : 0.f;
+        gl += pi;
+        go = fmaf(pi, __bfloat162float(vv[i]), go);
+      }
+      gm = mnew;
+      __syncthreads();  // sc / koff are refilled by the next chunk
+    }
+  }
+
   long long tot = 0, pre = 0;
   for (int i = t; i < p.groups; i += 128) {
     const long long n = (unit_need(p, i) + BN - 1) / BN;
@@ -728,15 +795,12 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   // The pass (and its partials) complete -- waited for by every block, so that the combine's completion implies
   // the pass's even when the pass finished every unit itself.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (nseg == 1 && extra_ml == nullptr && p.out != nullptr) return;  // finished by the pass
+  if (nseg == 1 && !gen.enabled && p.out != nullptr) return;  // finished by the pass
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + rh * p.st;
-  const float2* ml2 = extra_ml ? reinterpret_cast<const float2*>(extra_ml) + rh * extra_st : nullptr;
   // Segments that saw no key (sum 0) take no part, whatever their max.
-  float mx = -INFINITY;
+  float mx = gl > 0.f ? gm : -INFINITY;
   for (int s = 0; s < nseg; ++s)
     if (ml[s].y > 0.f) mx = fmaxf(mx, ml[s].x);
-  for (int s = 0; ml2 && s < extra_st; ++s)
-    if (ml2[s].y > 0.f) mx = fmaxf(mx, ml2[s].x);
   float o = 0.f, l = 0.f;
   if (mx != -INFINITY) {
     for (int s = 0; s < nseg; ++s) {
@@ -747,13 +811,10 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
         l = fmaf(wgt, e.y, l);
       }
     }
-    for (int s = 0; ml2 && s < extra_st; ++s) {
-      const float2 e = ml2[s];
-      if (e.y > 0.f) {
-        const float wgt = ex2(e.x - mx);
-        o = fmaf(wgt, extra_o[(rh * extra_st + s) * D + t], o);
-        l = fmaf(wgt, e.y, l);
-      }
+    if (gl > 0.f) {
+      const float wgt = ex2(gm - mx);
+      o = fmaf(wgt, go, o);
+      l = fmaf(wgt, gl, l);
     }
   }
   out[rh * D + t] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
@@ -872,8 +933,7 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   return cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, p);
 }
 
-cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o, const float* extra_ml, int extra_st,
-                              cudaStream_t stream) {
+cudaError_t launch_tc_combine(const TcParams& p, void* out, const GenKeys& gen, cudaStream_t stream) {
   using namespace tcattn;
   // Programmatic dependent launch: the combine's blocks start (and compute their unit's place) while the pass
   // drains, and wait for it (griddepcontrol.wait) before reading its partials.
@@ -888,10 +948,10 @@ cudaError_t launch_tc_combine(const TcParams& p, void* out, const float* extra_o
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_tc_kernel, p, p.grid, o, extra_o, extra_ml, extra_st);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_tc_kernel, p, p.grid, o, gen);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();  // no programmatic launch here: an ordinary one
-    combine_tc_kernel<<<cfg.gridDim, cfg.blockDim, 0, stream>>>(p, p.grid, o, extra_o, extra_ml, extra_st);
+    combine_tc_kernel<<<cfg.gridDim, cfg.blockDim, 0, stream>>>(p, p.grid, o, gen);
     e = cudaGetLastError();
   }
   return e;

@@ -204,7 +204,7 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
                                                  stride_pos, keys, t, stream),
                             "tensor-core attention launch"))
       return e;
-    return cuda_status(omni::launch_tc_combine(t, out, nullptr, nullptr, 0, stream), "combine launch");
+    return cuda_status(omni::launch_tc_combine(t, out, omni::GenKeys{}, stream), "combine launch");
   }
   const omni::SplitPlan plan = omni::plan_split(dtype, dim, groups, heads, nq, keys);
   const size_t need = omni::partial_bytes(rows_q, heads, plan.splits, dim);
@@ -309,11 +309,10 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
   b.qscale = scale * omni::kLog2e;
   b.status = status;
   if (omni::tc_path_enabled(dtype, dim, beams)) {
-    // Context keys on the tensor cores (one read per input for all its beams), generated keys gathered through
-    // the pointers on CUDA cores, one combine over both.
+    // Context keys on the tensor cores (one read per input for all its beams); the generated keys, gathered
+    // through the pointers, are attended by the combine itself while the pass runs, and merged with it.
     const int stc = omni::tc_segments(ctx_keys);
-    const size_t need_c = omni::partial_bytes(rows, heads, stc, dim);
-    const size_t need = need_c + omni::partial_bytes(rows, heads, pg.splits, dim);
+    const size_t need = omni::partial_bytes(rows, heads, stc, dim);
     if (!workspace || workspace_bytes < need || !aligned16(workspace))
       return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
                   workspace ? workspace_bytes : (size_t)0, need);
@@ -327,18 +326,23 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
     t.qscale = scale * omni::kLog2e;
     t.status = status;
     omni::carve_partials(workspace, rows, heads, stc, dim, &t.part_o, &t.part_ml);
-    float *go, *gml;
-    omni::carve_partials(static_cast<char*>(workspace) + need_c, rows, heads, 1, dim, &go, &gml);
     if (int e = cuda_status(omni::launch_tc_pass(kc, vc, ctx_rows, ctx_len_cap, ctx_stride_row, ctx_stride_head,
                                                  ctx_stride_pos, ctx_keys, t, stream),
                             "context attention launch"))
       return e;
-    b.part_o = go;
-    b.part_ml = gml;
-    b.st = 1;  // one partial per (row, head): a warp covers all of a row's generated keys
-    b.sp_offset = 0;
-    if (int e = cuda_status(omni::launch_gen_gather(b, (int)rows, stream), "generated-key launch")) return e;
-    return cuda_status(omni::launch_tc_combine(t, out, go, gml, 1, stream), "combine launch");
+    omni::GenKeys gk{};
+    gk.k = static_cast<const __nv_bfloat16*>(kg);
+    gk.v = static_cast<const __nv_bfloat16*>(vg);
+    gk.s_kb = gen_stride_row;
+    gk.s_kh = gen_stride_head;
+    gk.s_ks = gen_stride_pos;
+    gk.cache_rows = gen_rows;
+    gk.cache_len = gen_len_cap;
+    gk.ptr = ptr;
+    gk.ptr_stride = ptr_stride;
+    gk.gen_len = gen_len;
+    gk.enabled = 1;
+    return cuda_status(omni::launch_tc_combine(t, out, gk, stream), "combine launch");
   }
   const omni::SplitPlan pc = omni::plan_split(dtype, dim, groups, heads, beams, ctx_keys);
   const int st = pc.splits + pg.splits;
