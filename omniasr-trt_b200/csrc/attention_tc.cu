@@ -253,7 +253,8 @@ OMNI_DEV void issue_values(uint32_t tbase, int buf, const unsigned char* vslot, 
 template <int NQT, int SLOTS>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const __grid_constant__ CUtensorMap qmap, const Params pin) {
+                   const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap_half,
+                   const __grid_constant__ CUtensorMap vmap_half, const Params pin) {
   using L = Smem<SLOTS>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
@@ -344,6 +345,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const bool is_k = warp == 4;
       const CUtensorMap* map = is_k ? &kmap : &vmap;
+      const CUtensorMap* map_half = is_k ? &kmap_half : &vmap_half;  // 64-row boxes, for short unit tails
+      prefetch_tmap(map_half);
       TileIter ti = first_tile, ahead = first_tile;  // `ahead` runs p.prefetch tiles in front (into L2 early)
       for (int i = 0; i < p.prefetch && !ahead.done; ++i) ahead.advance();
       if (is_k) OMNI_TRACE_AT(4005);
@@ -373,9 +376,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[slot], SLOT_BYTES);
-        tma_load_4d(smem + slot * SLOT_BYTES, map, 0, tt * BN, h, ti.g, &full[slot]);
-        tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, map, 64, tt * BN, h, ti.g, &full[slot]);
+        // A unit's last tile with at most 64 keys left loads 64-row boxes: the rows past the keys are masked (K) or
+        // zeroed (V) by the softmax warps whatever they hold.
+        const bool short_tail = (int64_t)tt * BN + 64 >= ti.need;
+        const CUtensorMap* m = short_tail ? map_half : map;
+        mbar_arrive_expect_tx(&full[slot], short_tail ? SLOT_BYTES / 2 : SLOT_BYTES);
+        tma_load_4d(smem + slot * SLOT_BYTES, m, 0, tt * BN, h, ti.g, &full[slot]);
+        tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, m, 64, tt * BN, h, ti.g, &full[slot]);
         if (is_k) {
           issued_k = it + 1;
           OMNI_TRACE_AT(it * 8);
@@ -833,12 +840,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_cache_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int64_t len, int64_t s_row,
-                    int64_t s_head, int64_t s_pos) {
+                    int64_t s_head, int64_t s_pos, int box_rows = BN) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)rows};
   cuuint64_t strides[3] = {(cuuint64_t)s_pos * 2, (cuuint64_t)s_head * 2, (cuuint64_t)s_row * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)BN, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, OMNI_TC_L2_PROMOTION,
@@ -896,10 +903,12 @@ int tc_unit_cost() {
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream) {
   using namespace tcattn;
-  CUtensorMap kmap, vmap;
+  CUtensorMap kmap, vmap, kmap_half, vmap_half;
   CUtensorMap qmap;
   if (!make_cache_map(&kmap, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
       !make_cache_map(&vmap, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
+      !make_cache_map(&kmap_half, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, 64) ||
+      !make_cache_map(&vmap_half, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, 64) ||
       !make_query_map(&qmap, p.q, (int64_t)p.groups * p.nq, p.heads))
     return cudaErrorInvalidValue;
   p.cap = cache_len < keys ? cache_len : keys;
@@ -907,7 +916,7 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   p.grid = tc_grid();
   p.unit_cost = tc_unit_cost();
   p.prefetch = tc_prefetch();
-  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, Params);
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
   static const Kern table[5] = {attn_tc_kernel<1, 6>, attn_tc_kernel<2, 6>, attn_tc_kernel<4, 6>,
                                 attn_tc_kernel<8, 6>, attn_tc_kernel<16, 6>};
   const int ci = p.nq <= 1 ? 0 : p.nq <= 2 ? 1 : p.nq <= 4 ? 2 : p.nq <= 8 ? 3 : 4;
@@ -930,7 +939,7 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, p);
+  return cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, kmap_half, vmap_half, p);
 }
 
 cudaError_t launch_tc_combine(const TcParams& p, void* out, const GenKeys& gen, cudaStream_t stream) {
