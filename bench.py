@@ -87,9 +87,10 @@ def keys_bucket(n: int) -> int:
 class Workload:
     """One step of a BASELINE config through the public API (``omniasr_b200.kernels``), captured as a CUDA graph.
 
-    ``run(ev)`` issues the step's launches; with ``ev`` it records a pair of events around every launch of the
-    dominant (roofline) call. ``step_units`` is the algorithmic bytes (or FLOPs) of one step on this rank and
-    ``roof_units`` those of one roofline call."""
+    A step is ``layers`` layers (or cases); ``layer(i, ev)`` issues layer i's launches and returns the results a
+    caller reads back, with ``ev`` (a pair of events) recorded around the dominant (roofline) call, and
+    ``layer_in(i)`` names the device inputs layer i takes from the host in the end-to-end step. ``step_units`` is the
+    algorithmic bytes (or FLOPs) of one step on this rank and ``roof_units`` those of one roofline call."""
 
     name = ""
     metric = ""
@@ -106,14 +107,19 @@ class Workload:
         assert kernels.available(device), "needs a B200 (compute capability 10.0) and the built library"
         self.device, self.rank, self.world, self.layers = device, rank, world, layers
         self.gen = torch.Generator(device=device).manual_seed(1000 + rank)
-        self.h2d: list[torch.Tensor] = []  # inputs refreshed from pinned host memory every end-to-end step
-        self.d2h: list[torch.Tensor] = []  # results read back every end-to-end step
+        self.d2h: list[list[torch.Tensor]] = []  # per layer, the results read back in the end-to-end step
 
     def randn(self, *shape):
         return torch.randn(*shape, generator=self.gen, device=self.device, dtype=torch.bfloat16)
 
-    def run(self, ev=None):
+    def layer(self, i: int, ev=None) -> list[torch.Tensor]:
         raise NotImplementedError
+
+    def layer_in(self, i: int) -> list[torch.Tensor]:
+        return []
+
+    def run(self, ev=None):
+        self.d2h = [self.layer(i, ev[i] if ev else None) for i in range(self.layers)]
 
     def config(self) -> dict:
         raise NotImplementedError
@@ -167,19 +173,18 @@ class Verify(Workload):
         nb = self.bytes(lengths)
         self.step_units = nb["layer"] * self.layers
         self.roof_units = nb["attention"]
-        self.h2d = [self.qkv]
 
-    def run(self, ev=None):
-        outs = []
-        for i in range(self.layers):
-            q = self.K.rope_kv(self.qkv[i], self.cs, self.pos, self.kc[i], self.vc[i], H, self.slots)
-            if ev:
-                ev[i][0].record()
-            outs.append(self.K.draft_attention(q, self.kc[i], self.vc[i], self.att_len, self.T, self.keys, D**-0.5))
-            if ev:
-                ev[i][1].record()
-        self.d2h = outs
-        return outs
+    def layer_in(self, i):
+        return [self.qkv[i]]
+
+    def layer(self, i, ev=None):
+        q = self.K.rope_kv(self.qkv[i], self.cs, self.pos, self.kc[i], self.vc[i], H, self.slots)
+        if ev:
+            ev[0].record()
+        o = self.K.draft_attention(q, self.kc[i], self.vc[i], self.att_len, self.T, self.keys, D**-0.5)
+        if ev:
+            ev[1].record()
+        return [o]
 
     def config(self):
         return {"workload": "BASELINE config 2: spec-4 verify attention + fused RoPE/KV append, batch 8 per GPU, "
@@ -236,18 +241,17 @@ class Decode(Workload):
         self.lengths = torch.full((B,), L, dtype=torch.int64, device=self.device)
         self.roof_units = B * L * KV_TOKEN + 2 * B * H * D * 2
         self.step_units = self.roof_units * self.layers
-        self.h2d = [self.q]
 
-    def run(self, ev=None):
-        outs = []
-        for i in range(self.layers):
-            if ev:
-                ev[i][0].record()
-            outs.append(self.K.decode_attention(self.q[i], self.kc[i], self.vc[i], self.lengths, self.L, D**-0.5))
-            if ev:
-                ev[i][1].record()
-        self.d2h = outs
-        return outs
+    def layer_in(self, i):
+        return [self.q[i]]
+
+    def layer(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        o = self.K.decode_attention(self.q[i], self.kc[i], self.vc[i], self.lengths, self.L, D**-0.5)
+        if ev:
+            ev[1].record()
+        return [o]
 
     def config(self):
         return {"workload": "BASELINE config 1: decode attention, batch 8 per GPU, q_len 1, 32x128 heads, 1024 keys "
@@ -310,19 +314,18 @@ class Beam(Workload):
         self.gen_len = torch.full((rows,), self.GEN, dtype=torch.int64, device=self.device)
         self.roof_units = self.bytes(ctx)
         self.step_units = self.roof_units * self.layers
-        self.h2d = [self.q]
 
-    def run(self, ev=None):
-        outs = []
-        for i in range(self.layers):
-            if ev:
-                ev[i][0].record()
-            outs.append(self.K.beam_attention(self.q[i], self.kc[i], self.vc[i], self.ctx, self.kg[i], self.vg[i],
-                                              self.ptr, self.gen_len, self.N, self.ctx_keys, D**-0.5))
-            if ev:
-                ev[i][1].record()
-        self.d2h = outs
-        return outs
+    def layer_in(self, i):
+        return [self.q[i]]
+
+    def layer(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        o = self.K.beam_attention(self.q[i], self.kc[i], self.vc[i], self.ctx, self.kg[i], self.vg[i], self.ptr,
+                                  self.gen_len, self.N, self.ctx_keys, D**-0.5)
+        if ev:
+            ev[1].record()
+        return [o]
 
     def config(self):
         return {"workload": "BASELINE config 3 (attention): 8 inputs x 5 beams = 40 rows per GPU, q_len 1, 32x128, "
@@ -377,19 +380,20 @@ class Gather(Workload):
         self.row_bytes = H * self.CAP * D * 2
         self.roof_units = 2 * rows * self.row_bytes  # read + write of one tensor
         self.step_units = 2 * self.roof_units * self.layers
-        self.h2d = [self.parent]
         self.calls_per_layer = 2
 
-    def run(self, ev=None):
-        for i in range(self.layers):
-            for t in range(2):
-                if ev and t == 0:
-                    ev[i][0].record()
-                self.K.reorder_gather(self.src[i][t], self.parent, self.dst[t])
-                if ev and t == 0:
-                    ev[i][1].record()
-        self.d2h = [self.dst[0][:, 0, 0, :8]]  # a few bytes of each gathered row: the step's visible result
-        return self.dst
+    def layer_in(self, i):
+        return [self.parent] if i == 0 else []
+
+    def layer(self, i, ev=None):
+        for t in range(2):
+            if ev and t == 0:
+                ev[0].record()
+            self.K.reorder_gather(self.src[i][t], self.parent, self.dst[t])
+            if ev and t == 0:
+                ev[1].record()
+        # a few bytes of each gathered row after the last source: the step's visible result
+        return [self.dst[0][:, 0, 0, :8]] if i == self.layers - 1 else []
 
     def config(self):
         return {"workload": "BASELINE config 3 (reorder): K and V cache rows [40, 32, 2048, 128] bf16 gathered by "
@@ -433,20 +437,18 @@ class Prefill(Workload):
         self.vc = [self.randn(B, H, self.CAP, D) for _ in range(self.layers)]
         self.roof_units = 4 * (W * (W + 1) // 2) * D * B * H  # QK^T and PV over the causal half (incl. diagonal)
         self.step_units = self.roof_units * self.layers
-        self.h2d = [self.q]
 
-    def run(self, ev=None):
-        outs = []
-        for i in range(self.layers):
-            q = self.q[i].view(self.B, self.W, H, D).transpose(1, 2)
-            if ev:
-                ev[i][0].record()
-            o = self.K.prefill_attention(q, self.kc[i][:, :, :self.W], self.vc[i][:, :, :self.W], D**-0.5)
-            if ev:
-                ev[i][1].record()
-            outs.append(o)
-        self.d2h = outs
-        return outs
+    def layer_in(self, i):
+        return [self.q[i]]
+
+    def layer(self, i, ev=None):
+        q = self.q[i].view(self.B, self.W, H, D).transpose(1, 2)
+        if ev:
+            ev[0].record()
+        o = self.K.prefill_attention(q, self.kc[i][:, :, :self.W], self.vc[i][:, :, :self.W], D**-0.5)
+        if ev:
+            ev[1].record()
+        return [o]
 
     def config(self):
         return {"workload": "BASELINE config 4 (prefill attention): 8 rows x 1500 frames per GPU, causal, 32x128 "
@@ -495,22 +497,24 @@ class Sweep(Workload):
         self.roof_units = self.case_bytes[-1]
         self.step_units = sum(self.case_bytes)
         self.n = {L: torch.full((self.rows,), L, dtype=torch.int64, device=self.device) for _, L in self.CASES}
-        self.h2d = [self.q[1], self.q[5]]
 
-    def run(self, ev=None):
-        outs = []
-        for i, (t, L) in enumerate(self.CASES):
-            n, keys = self.n[L], self.keys[i]
-            if ev:
-                ev[i][0].record()
-            if t == 1:
-                outs.append(self.K.decode_attention(self.q[1], self.kc, self.vc, n, keys, D**-0.5))
-            else:
-                outs.append(self.K.draft_attention(self.q[5], self.kc, self.vc, n, t, keys, D**-0.5))
-            if ev:
-                ev[i][1].record()
-        self.d2h = outs
-        return outs
+    def layer_in(self, i):
+        t = self.CASES[i][0]
+        first = next(j for j, c in enumerate(self.CASES) if c[0] == t)
+        return [self.q[t]] if i == first else []
+
+    def layer(self, i, ev=None):
+        t, L = self.CASES[i]
+        n, keys = self.n[L], self.keys[i]
+        if ev:
+            ev[0].record()
+        if t == 1:
+            o = self.K.decode_attention(self.q[1], self.kc, self.vc, n, keys, D**-0.5)
+        else:
+            o = self.K.draft_attention(self.q[5], self.kc, self.vc, n, t, keys, D**-0.5)
+        if ev:
+            ev[1].record()
+        return [o]
 
     def config(self):
         return {"workload": "BASELINE config 5: 64 rows in all, sharded evenly over the GPUs, 32x128 heads; cases "
@@ -560,22 +564,21 @@ class Gemm(Workload):
         per_layer = 2 * (3 * Dm * Dm + Dm * Dm + 2 * Fn * Dm + Dm * Fn)
         self.roof_units = 2 * 3 * Dm * Dm
         self.step_units = per_layer * self.layers
-        self.h2d = [self.x]
 
-    def run(self, ev=None):
-        outs = []
-        for i in range(self.layers):
-            qkv_w, out_w, gi_w, ffo_w = self.w[i]
-            if ev:
-                ev[i][0].record()
-            outs.append(self.K.decode_gemm(self.x, qkv_w))
-            if ev:
-                ev[i][1].record()
-            outs.append(self.K.decode_gemm(self.o, out_w, "residual", residual=self.h))
-            outs.append(self.K.decode_gemm(self.x, gi_w, "swiglu"))
-            outs.append(self.K.decode_gemm(self.g, ffo_w, "residual", residual=self.h))
-        self.d2h = outs[-1:]
-        return outs
+    def layer_in(self, i):
+        return [self.x] if i == 0 else []
+
+    def layer(self, i, ev=None):
+        qkv_w, out_w, gi_w, ffo_w = self.w[i]
+        if ev:
+            ev[0].record()
+        self.K.decode_gemm(self.x, qkv_w)
+        if ev:
+            ev[1].record()
+        self.K.decode_gemm(self.o, out_w, "residual", residual=self.h)
+        self.K.decode_gemm(self.x, gi_w, "swiglu")
+        last = self.K.decode_gemm(self.g, ffo_w, "residual", residual=self.h)
+        return [last] if i == self.layers - 1 else []
 
     def run_library(self):
         """The same GEMMs as the reference computes them (torch / cuBLAS)."""
@@ -733,18 +736,48 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     case_ms = [max_over_ranks(x) for x in per_call] if args.workload == "sweep" else None
 
     # --- end to end through the public API: inputs from pinned host memory, results back, every step ---
-    hosts_in = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in wl.h2d]
-    for h, t in zip(hosts_in, wl.h2d):
-        h.copy_(t.cpu())
-    hosts_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in wl.d2h]
+    # One graph per step: layer i's inputs are copied in on an input copy stream, its launches run on the capture
+    # stream once they have arrived, and its results are copied out on an output copy stream, so the copies of
+    # other layers overlap the kernels (two copy engines, one per direction). Replays are stream-ordered: a step
+    # starts after the previous step's last result has reached the host.
+    hosts_in = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in wl.layer_in(i)] for i in range(wl.layers)]
+    for i, hs in enumerate(hosts_in):
+        for h, t in zip(hs, wl.layer_in(i)):
+            h.copy_(t.cpu())
+    hosts_out = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs] for outs in wl.d2h]
     stream = torch.cuda.current_stream(device)
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    graph_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        graph_e2e.capture_begin()
+        copy_in.wait_stream(side)
+        copy_out.wait_stream(side)
+        arrived = []
+        with torch.cuda.stream(copy_in):
+            for i, hs in enumerate(hosts_in):
+                for h, t in zip(hs, wl.layer_in(i)):
+                    t.copy_(h, non_blocking=True)
+                arrived.append(torch.cuda.Event())
+                arrived[-1].record(copy_in)
+        e2e_outs = []
+        for i in range(wl.layers):
+            side.wait_event(arrived[i])
+            outs = wl.layer(i)
+            e2e_outs.append(outs)
+            done = torch.cuda.Event()
+            done.record(side)
+            copy_out.wait_event(done)
+            with torch.cuda.stream(copy_out):
+                for h, t in zip(hosts_out[i], outs):
+                    h.copy_(t, non_blocking=True)
+        side.wait_stream(copy_in)
+        side.wait_stream(copy_out)
+        graph_e2e.capture_end()
+    stream.wait_stream(side)
+    torch.cuda.synchronize(device)
 
     def e2e_step():
-        for h, t in zip(hosts_in, wl.h2d):
-            t.copy_(h, non_blocking=True)
-        graph.replay()
-        for h, t in zip(hosts_out, wl.d2h):
-            h.copy_(t, non_blocking=True)
+        graph_e2e.replay()
 
     for _ in range(args.warmup):
         e2e_step()
@@ -775,10 +808,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": dict(wl.config(), parallelism=f"request-sharded dp{world} (no collective)"),
         "e2e": {"value": round(world * wl.step_units / (e2e_ms / args.steps * 1e-3) / scale, 1), "unit": wl.unit,
                 "ms_per_step": round(e2e_ms / args.steps, 4),
-                "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in hosts_in)),
-                "d2h_bytes_per_step": int(sum(t.numel() * t.element_size() for t in hosts_out)),
-                "path": "omniasr_b200.kernels calls captured in a CUDA graph; inputs copied in from pinned host "
-                        "memory and results copied out every step"},
+                "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for hs in hosts_in for t in hs)),
+                "d2h_bytes_per_step": int(sum(t.numel() * t.element_size() for hs in hosts_out for t in hs)),
+                "path": "omniasr_b200.kernels calls captured in one CUDA graph per step: every layer's inputs copied "
+                        "in from pinned host memory and its results copied out, on two copy streams overlapping the "
+                        "other layers' kernels; steps do not overlap"},
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": peak,
                      "unit": "TFLOP/s" if wl.bound == "tensor" else "GB/s", "frac": round(achieved / peak, 3),
                      "peak_kind": pk["kind"], "kernel": wl.roof_kernel, "traffic": traffic_per_launch(wl.traffic_key),

@@ -891,13 +891,16 @@ int tc_prefetch() {
   return n < 0 ? 0 : n;
 }
 
-// Cost of a unit's start and epilogue in tile-eighths (OMNIASR_TC_UNIT_COST overrides the default of one tile).
-int tc_unit_cost() {
+// Cost of a unit's start and epilogue in tile-eighths. Measured on B200 (config-2 and config-1 shapes): units of
+// several query rows split best at one tile (8), single-query units at 0 -- their epilogue is short, and a finer
+// split evens out the CTAs' ends. OMNIASR_TC_UNIT_COST overrides both.
+int tc_unit_cost(int nq) {
   static const int c = [] {
     const char* e = getenv("OMNIASR_TC_UNIT_COST");
-    return e ? atoi(e) : 8;
+    return e ? atoi(e) : -1;
   }();
-  return c < 0 ? 0 : c;
+  if (c >= 0) return c;
+  return nq <= 1 ? 0 : 8;
 }
 
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
@@ -914,7 +917,7 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   p.cap = cache_len < keys ? cache_len : keys;
   p.st = tc_segments(keys);
   p.grid = tc_grid();
-  p.unit_cost = tc_unit_cost();
+  p.unit_cost = tc_unit_cost(p.nq);
   p.prefetch = tc_prefetch();
   using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
   static const Kern table[5] = {attn_tc_kernel<1, 6>, attn_tc_kernel<2, 6>, attn_tc_kernel<4, 6>,
