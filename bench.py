@@ -133,10 +133,10 @@ class Verify(Workload):
 
     name = "verify"
     metric = "decode-attn HBM GB/s (spec-4 verify + fused RoPE/KV append, batch 8, 12 layers)"
-    roof_kernel = "draft_attention (split + combine launches of one layer)"
+    roof_kernel = "draft_attention (the pass of one layer, split units merged inside it)"
     traffic_key = "draft_attention_config2_bytes_per_call"
     B, T, CAP = 8, 5, 4096
-    calls_per_layer = 3  # rope_kv, attention pass, combine
+    calls_per_layer = 2  # rope_kv, attention pass (it merges split units itself)
 
     @classmethod
     def lengths(cls) -> torch.Tensor:
@@ -227,10 +227,10 @@ class Decode(Workload):
 
     name = "decode"
     metric = "decode-attn HBM GB/s (q_len 1, batch 8, 1024 keys, 12 layers)"
-    roof_kernel = "decode_attention (split + combine launches of one layer)"
+    roof_kernel = "decode_attention (the pass of one layer, split units merged inside it)"
     traffic_key = "decode_attention_config1_bytes_per_call"
     B, L = 8, 1024
-    calls_per_layer = 2
+    calls_per_layer = 1
 
     def __init__(self, *a):
         super().__init__(*a)
@@ -281,10 +281,10 @@ class Beam(Workload):
 
     name = "beam"
     metric = "beam-attn HBM GB/s (8 inputs x 5 beams, context U[300,1800], 12 layers)"
-    roof_kernel = "beam_attention (context, generated and combine launches of one layer)"
+    roof_kernel = "beam_attention (context pass and combine of one layer; the combine attends the generated keys)"
     traffic_key = "beam_attention_config3_bytes_per_call"
     S, N, CAP, G, GEN = 8, 5, 2048, 64, 32
-    calls_per_layer = 3  # context pass (tensor cores), generated-key pass, combine
+    calls_per_layer = 2  # context pass (tensor cores), combine (with the generated keys)
 
     @classmethod
     def draw(cls):
@@ -480,7 +480,7 @@ class Sweep(Workload):
     roof_kernel = "draft_attention (q_len 5, 8192 keys)"
     traffic_key = "draft_attention_config5_bytes_per_call"
     ROWS, CASES = 64, [(1, 512), (1, 2048), (1, 8192), (5, 512), (5, 2048), (5, 8192)]
-    calls_per_layer = 2
+    calls_per_layer = 1
 
     def __init__(self, device, rank, world, layers):
         super().__init__(device, rank, world, len(self.CASES))
@@ -1041,7 +1041,7 @@ def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict |
                      "frac": round(nbytes / (steps_ms / steps * 1e-3) / 1e9 / pk["hbm"], 3),
                      "peak_kind": pk["kind"], "kernel": "whole decoder step (weights + K/V read once)",
                      "traffic": None, "bytes_per_step": nbytes},
-        "gpu_launches": (3 * LAYERS + 2) * steps if ours else 0,  # rope_kv, pass, combine per layer; propose, accept
+        "gpu_launches": (2 * LAYERS + 2) * steps if ours else 0,  # rope_kv, pass per layer; propose, accept
         "clocks": clock,
     }
     return line

@@ -63,7 +63,15 @@ int omniasr_splits_for(int rows, int heads, int keys, int block, int programs, i
 /* Bytes of workspace an attention call of this shape needs on the current device (the split
  * partials; the reference allocates them inside its wrappers, omniasr_trt/kernels.py:319-320,
  * :349-350, :416-417). kind: OMNIASR_DECODE (per_group = 1), OMNIASR_DRAFT (per_group = tokens),
- * OMNIASR_BEAM (per_group = beams, gen_keys = generated-cache length). */
+ * OMNIASR_BEAM (per_group = beams, gen_keys = generated-cache length).
+ *
+ * Decode and draft workspaces begin with OMNIASR_ATTENTION_COUNTER_BYTES of per-(row, head) counters
+ * through which the last CTA to finish a row's keys merges the partial results itself (no second
+ * kernel). Those bytes must be zero before the workspace's first use, and every call leaves them
+ * zero: zero a workspace once when allocating it and reuse it for calls in stream order. Calls that
+ * may overlap on the GPU need workspaces of their own. After status bit 2 (a wait gave up) the
+ * counters may be left non-zero: zero them again. The beam workspace has no counters. */
+#define OMNIASR_ATTENTION_COUNTER_BYTES 65536
 size_t omniasr_attention_workspace(int kind, int dtype, int groups, int per_group, int heads, int dim,
                                    int64_t keys, int64_t gen_keys);
 
@@ -179,7 +187,8 @@ int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w
  * only the input and output buffers. Shapes whose split partials exceed the array are rejected with
  * OMNIASR_ERR_WORKSPACE. The first call on a device looks up the array's address (cudaGetSymbolAddress) and
  * should come before any stream capture. All calls on a device share the array: calls whose kernels overlap on
- * the GPU race, so order them (same stream, or events). */
+ * the GPU race, so order them (same stream, or events). The array's leading unit counters start at zero (a
+ * static device array is zero-initialised when the library loads) and every call leaves them zero. */
 int omniasr_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
                                      int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
                                      const int64_t* lengths, void* out, int batch, int heads, int dim, int keys,

@@ -72,8 +72,15 @@ struct TcParams {
   int prefetch;   // tiles prefetched into L2 ahead of the loads (set by launch_tc_pass)
   __nv_bfloat16* out;  // [groups * nq, heads, 128]: units a single CTA finishes are written here directly
                        // (null: every unit goes through the combine, e.g. when a second pass adds partials)
+  unsigned* counters;  // [groups * heads] segments published per unit, zero on entry and left zero; non-null (with
+                       // out): the last CTA to finish a unit merges its segments itself and no combine runs
   int* status;
 };
+
+// Decode / draft workspaces start with kCounterBytes of unit counters (zero before the first call, left zero by
+// every call), then the split partials. Shapes with more than kCounterUnits (group, head) units merge in a combine.
+constexpr int kCounterUnits = 16384;
+constexpr size_t kCounterBytes = kCounterUnits * sizeof(unsigned);
 
 bool tc_path_enabled(int dtype, int dim, int nq);
 int tc_segments(int64_t keys);

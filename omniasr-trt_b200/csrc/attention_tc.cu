@@ -218,6 +218,82 @@ OMNI_DEV bool named_sync_or(int id, int count, bool pred) {
   return out != 0;
 }
 
+OMNI_DEV unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Four output dims a * inv as bf16.
+OMNI_DEV void store_out4(__nv_bfloat16* dst, const float4& a, float inv) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x * inv, a.y * inv);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z * inv, a.w * inv);
+  uint2 w;
+  w.x = *reinterpret_cast<const uint32_t*>(&lo);
+  w.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(dst) = w;
+}
+
+// Output rows of unit (g, h) from its nseg segments: segment `own` from this CTA's stash, the others' from the
+// partial arrays (read through L2: other CTAs wrote them). One warp; lane l holds dims 4l .. 4l+3. Segments go
+// outermost so that a chunk of queries has all its loads of one segment in flight at once; the merge is the
+// combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max), segments that saw no key take no part.
+template <int NQT>
+OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int lane, const float* red_l,
+                         const float* stash_m, const float* stash) {
+  constexpr int JC = NQT < 8 ? NQT : 8;  // queries per chunk (register budget)
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
+#pragma unroll 1
+  for (int j0 = 0; j0 < NQT && j0 < p.nq; j0 += JC) {
+    float m[JC], l[JC];
+    float4 o[JC];
+#pragma unroll
+    for (int c = 0; c < JC; ++c) {
+      const int j = j0 + c;
+      l[c] = j < p.nq ? red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j] : 0.f;
+      m[c] = l[c] > 0.f ? stash_m[j] : -INFINITY;
+      o[c] = l[c] > 0.f ? *reinterpret_cast<const float4*>(stash + j * D + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 1
+    for (int s = 0; s < nseg; ++s) {
+      if (s == own) continue;
+      float2 e[JC];
+      float4 v[JC];
+#pragma unroll
+      for (int c = 0; c < JC; ++c) {
+        const int j = j0 + c;
+        if (j < p.nq) {
+          const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
+          e[c] = __ldcg(ml + part);
+          v[c] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * D) + lane);
+        } else {
+          e[c] = make_float2(0.f, 0.f);
+          v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < JC; ++c) {
+        if (e[c].y > 0.f) {
+          const float mn = fmaxf(m[c], e[c].x);
+          const float a = ex2(m[c] - mn), b = ex2(e[c].x - mn);
+          o[c] = make_float4(fmaf(o[c].x, a, v[c].x * b), fmaf(o[c].y, a, v[c].y * b), fmaf(o[c].z, a, v[c].z * b),
+                             fmaf(o[c].w, a, v[c].w * b));
+          l[c] = fmaf(l[c], a, e[c].y * b);
+          m[c] = mn;
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < JC; ++c) {
+      const int j = j0 + c;
+      if (j < p.nq) {
+        const int64_t rowh = ((int64_t)g * p.nq + j) * p.heads + h;
+        store_out4(p.out + rowh * D + 4 * lane, o[c], l[c] > 0.f ? 1.f / l[c] : 0.f);
+      }
+    }
+  }
+}
+
 // S^T[buf] = K_tile (slot ks) . Q^T  (thread 0).
 OMNI_DEV void issue_scores(uint32_t tbase, int buf, const unsigned char* kslot, const unsigned char* qs) {
   const uint32_t kaddr = smem_addr(kslot);
@@ -318,6 +394,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     p.lengths = s_len;
   }
   if (tid == 0) OMNI_TRACE_AT(4003);
+  const bool merge_here = p.counters != nullptr && p.out != nullptr;  // no combine kernel follows
+  if (merge_here) {
+    // What the combine would otherwise do for the units without a segment: report lengths outside the cache and
+    // give the rows that see no key zeros (their units have no tiles, so no CTA of the pass visits them).
+    if (blockIdx.x == 0) {
+      for (int g = tid; g < p.groups; g += THREADS) {
+        const int64_t raw = p.lengths[g] + (p.causal ? p.nq - 1 : 0);
+        if (p.lengths[g] < 0 || raw > p.cap) raise_status(p.status, kStatusIndex);
+      }
+    }
+    if (warp == 7) {
+      for (int g = blockIdx.x; g < p.groups; g += gridDim.x) {
+        if (unit_need(p, g) > 0) continue;
+        uint4* o = reinterpret_cast<uint4*>(p.out + (int64_t)g * p.nq * p.heads * D);
+        for (int i = lane; i < p.nq * p.heads * (D / 8); i += 32) o[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
 
   const int64_t total = total_cost(p);
   if (tid == 0) OMNI_TRACE_AT(4007);
@@ -640,25 +734,45 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       const int64_t pos0 = ti.unit_pos0();
-      const int seg = (int)(blockIdx.x - pos0 / per);
-      const bool whole = (pos0 + kTileCost * (ti.tiles - 1)) / per == pos0 / per;
-      for (int j = 0; j < p.nq && j < NQT; ++j) {
-        const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
-        const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
-        const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-        if (whole && p.out) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x * inv, a.y * inv);
-          const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z * inv, a.w * inv);
-          uint2 w;
-          w.x = *reinterpret_cast<const uint32_t*>(&lo);
-          w.y = *reinterpret_cast<const uint32_t*>(&hi);
-          *reinterpret_cast<uint2*>(p.out + rowh * D + 4 * lane) = w;
-        } else {
-          const int64_t part = rowh * p.st + seg;
-          *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
-          if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+      const int64_t seg0 = pos0 / per;  // the unit's first CTA
+      const int seg = (int)(blockIdx.x - seg0);
+      const int nseg = (int)((pos0 + kTileCost * (ti.tiles - 1)) / per - seg0 + 1);
+      const bool whole = nseg == 1;
+      // In-pass merge of a unit cut between CTAs: the segments are counted per unit; the CTA that finds the others
+      // all published (one acquire load) merges at once from its stash without publishing its own, else it
+      // publishes and counts, and the last to count merges.
+      unsigned* ctr = merge_here && !whole ? p.counters + (int64_t)ti.g * p.heads + ti.h : nullptr;
+      bool last = false;
+      if (ctr) {
+        unsigned c = 0;
+        if (lane == 0) c = ld_acquire_gpu(ctr);
+        last = __shfl_sync(0xffffffffu, c, 0) == (unsigned)(nseg - 1);
+      }
+      if (!last) {
+        for (int j = 0; j < p.nq && j < NQT; ++j) {
+          const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
+          const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
+          const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
+          if (whole && p.out) {
+            store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
+          } else {
+            const int64_t part = rowh * p.st + seg;
+            *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
+            if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+          }
         }
+        if (ctr) {
+          __threadfence();  // this lane's partial stores before the count
+          __syncwarp();
+          unsigned old = 0;
+          if (lane == 0) old = atomicAdd(ctr, 1u);
+          last = __shfl_sync(0xffffffffu, old, 0) == (unsigned)(nseg - 1);
+        }
+      }
+      if (last) {
+        __threadfence();  // the other CTAs' partials after their counts
+        merge_unit<NQT>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
+        if (lane == 0) *ctr = 0;  // zero again for the next call
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&seg_free);

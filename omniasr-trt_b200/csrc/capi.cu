@@ -14,6 +14,8 @@
 #include "spec.cuh"
 #include "wgemm.cuh"
 
+static_assert(omni::kCounterBytes == OMNIASR_ATTENTION_COUNTER_BYTES, "counter prefix of the decode / draft workspace");
+
 namespace {
 
 thread_local std::string g_error;
@@ -83,7 +85,7 @@ int set_last_error(int code, const char* message) { return fail(code, "%s", mess
 
 extern "C" {
 
-int omniasr_abi_version(void) { return 1; }
+int omniasr_abi_version(void) { return 2; }
 
 const char* omniasr_last_error(void) { return g_error.c_str(); }
 
@@ -125,9 +127,11 @@ size_t omniasr_attention_workspace(int kind, int dtype, int groups, int per_grou
     const omni::SplitPlan c = omni::plan_split(dtype, dim, groups, heads, per_group, keys);
     return omni::partial_bytes(rows_q, heads, c.splits + g.splits, dim);
   }
-  if (omni::tc_path_enabled(dtype, dim, nq)) return omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
+  // Decode and draft workspaces: the unit counters, then the partials.
+  if (omni::tc_path_enabled(dtype, dim, nq))
+    return omni::kCounterBytes + omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
   const omni::SplitPlan p = omni::plan_split(dtype, dim, groups, heads, nq, keys);
-  return omni::partial_bytes(rows_q, heads, p.splits, dim);
+  return omni::kCounterBytes + omni::partial_bytes(rows_q, heads, p.splits, dim);
 }
 
 int omniasr_rope_kv(const void* qkv, int64_t qkv_stride, const float* cs, int64_t cs_positions, const int64_t* pos,
@@ -185,7 +189,7 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
     return fail(OMNIASR_ERR_ARGUMENT, "%s: keys %d outside [0, cache length %lld]", name, keys, (long long)cache_len);
   const int64_t rows_q = (int64_t)groups * nq;
   if (omni::tc_path_enabled(dtype, dim, nq)) {
-    const size_t need = omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
+    const size_t need = omni::kCounterBytes + omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);
     if (!workspace || workspace_bytes < need || !aligned16(workspace))
       return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
                   workspace ? workspace_bytes : (size_t)0, need);
@@ -199,20 +203,25 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
     t.qscale = scale * omni::kLog2e;
     t.status = status;
     t.out = static_cast<__nv_bfloat16*>(out);
-    omni::carve_partials(workspace, rows_q, heads, omni::tc_segments(keys), dim, &t.part_o, &t.part_ml);
+    // The last CTA to finish a unit merges its segments (no combine kernel) when the unit counters cover the shape.
+    t.counters = (int64_t)groups * heads <= omni::kCounterUnits ? static_cast<unsigned*>(workspace) : nullptr;
+    omni::carve_partials(static_cast<char*>(workspace) + omni::kCounterBytes, rows_q, heads, omni::tc_segments(keys),
+                         dim, &t.part_o, &t.part_ml);
     if (int e = cuda_status(omni::launch_tc_pass(k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
                                                  stride_pos, keys, t, stream),
                             "tensor-core attention launch"))
       return e;
+    if (t.counters) return ok();
     return cuda_status(omni::launch_tc_combine(t, out, omni::GenKeys{}, stream), "combine launch");
   }
   const omni::SplitPlan plan = omni::plan_split(dtype, dim, groups, heads, nq, keys);
-  const size_t need = omni::partial_bytes(rows_q, heads, plan.splits, dim);
+  const size_t need = omni::kCounterBytes + omni::partial_bytes(rows_q, heads, plan.splits, dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
                 workspace ? workspace_bytes : (size_t)0, need);
   float *po, *pml;
-  omni::carve_partials(workspace, rows_q, heads, plan.splits, dim, &po, &pml);
+  omni::carve_partials(static_cast<char*>(workspace) + omni::kCounterBytes, rows_q, heads, plan.splits, dim, &po,
+                       &pml);
   omni::SplitArgs a{};
   a.q = q;
   a.k = k_cache;

@@ -12,9 +12,10 @@
 // cudaGetSymbolAddress (a host-side symbol is not a device pointer) and caches it per device; make that first
 // call outside any stream capture. Every later call on the device reuses the cached address.
 //
-// Sharing: all calls on a device use the same array and it keeps the previous call's contents. No value
-// needs to start at zero (a call writes every partial it reads before reading it), but two calls whose
-// kernels overlap on the GPU (different streams without ordering) race on the array: order them.
+// Sharing: all calls on a device use the same array and it keeps the previous call's contents. Only its
+// leading unit counters must start at zero: a static device array is zero-initialised when the module loads,
+// and every call leaves the counters zero (a call writes every partial it reads before reading it). Two calls
+// whose kernels overlap on the GPU (different streams without ordering) race on the array: order them.
 
 #include <stdio.h>
 

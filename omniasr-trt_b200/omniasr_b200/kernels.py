@@ -16,9 +16,10 @@ CUDA-graph capture run on these kernels unchanged:
   ``beam.py:175-176``).
 
 Each call is a launch (or two) of hand-written CUDA through the C ABI of ``include/omniasr_b200.h`` on the
-current stream; outputs and split workspaces are allocated with ``torch.empty`` on the caller's device (from the
-graph pool during a capture). There is no other code path: on a CUDA device without the built library every
-function raises.
+current stream; outputs and the beam search's split workspace are allocated with ``torch.empty`` on the caller's
+device (from the graph pool during a capture); decode and draft calls reuse one zeroed workspace per stream, whose
+leading unit counters let the pass merge split units itself. There is no other code path: on a CUDA device without
+the built library every function raises.
 """
 
 from __future__ import annotations
@@ -62,11 +63,17 @@ def status_word(device: torch.device | int | None = None) -> torch.Tensor:
 
 
 def read_status(device=None, clear: bool = True) -> int:
-    """Synchronises, returns the status word and clears it."""
+    """Synchronises, returns the status word and clears it. After a wait that gave up (bit 2) the unit counters of
+    the decode / draft workspaces may be left non-zero, so those workspaces are dropped (the next call zeroes a
+    new one)."""
     word = status_word(device)
     value = int(word.item())
     if clear:
         word.zero_()
+    if value & 2:
+        index = word.device.index
+        for key in [k for k in _ATTN_WS if k[0] == index]:
+            _ATTN_WS_RETIRED.append(_ATTN_WS.pop(key))
     return value
 
 
@@ -104,6 +111,24 @@ def _cache(k: torch.Tensor, v: torch.Tensor, name: str) -> tuple:
 
 def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+_ATTN_WS: dict = {}  # (device, stream) -> decode / draft workspace; its unit counters start zero and stay zero
+_ATTN_WS_RETIRED: list = []  # outgrown workspaces, kept alive for CUDA graphs that captured them
+
+
+def _attn_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """The decode / draft workspace of the current stream: zeroed once when allocated (its leading unit counters
+    must be zero on entry, and every call leaves them zero), reused by the stream's calls in order."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _ATTN_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _ATTN_WS_RETIRED.append(ws)
+        with torch.inference_mode(False):
+            ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+        _ATTN_WS[key] = ws
+    return ws
 
 
 def rope_kv(qkv: torch.Tensor, cs: torch.Tensor, pos: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -148,7 +173,7 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     lengths = _index(lengths)
     lib = _lib.load()
     nbytes = lib.omniasr_attention_workspace(_lib.DECODE, dtype, b, 1, heads, dim, keys, 0)
-    ws = _workspace(nbytes, q.device)
+    ws = _attn_workspace(nbytes, q.device)
     _lib.call("omniasr_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), rows, length, s_row, s_head, s_pos,
               _ptr(lengths), _ptr(out), b, heads, dim, int(keys), float(scale), dtype, _ptr(ws), ws.numel(),
               _ptr(status_word(q.device)), _stream(q.device))
@@ -174,7 +199,7 @@ def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     lengths = _index(lengths)
     lib = _lib.load()
     nbytes = lib.omniasr_attention_workspace(_lib.DRAFT, dtype, b, tokens, heads, dim, keys, 0)
-    ws = _workspace(nbytes, q.device)
+    ws = _attn_workspace(nbytes, q.device)
     _lib.call("omniasr_draft_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), rows, length, s_row, s_head, s_pos,
               _ptr(lengths), _ptr(out), b, int(tokens), heads, dim, int(keys), float(scale), dtype, _ptr(ws),
               ws.numel(), _ptr(status_word(q.device)), _stream(q.device))

@@ -38,7 +38,7 @@ def test_exported_symbols_in_the_shared_object():
 
 def test_abi_version_and_no_error_message():
     lib = _lib.load()
-    assert lib.omniasr_abi_version() == 1
+    assert lib.omniasr_abi_version() == 2
     assert isinstance(lib.omniasr_last_error(), bytes)
 
 

@@ -419,6 +419,101 @@ def test_tc_attention_uninitialised_cache_tail_is_ignored(K):
     check_attention(out, oatt.decode_attention(q, kz, vz, lengths, d**-0.5), torch.bfloat16, what="nan tail")
 
 
+# In-pass merge: the last CTA to finish a (row, head) unit merges the unit's segments through the unit counters at the
+# head of the decode / draft workspace (no combine kernel); those counters must be zero again after every call.
+
+def _counters_zero(K):
+    ws = K._ATTN_WS[(torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)]
+    torch.cuda.synchronize()
+    return not ws[:65536].any()
+
+
+@pytest.mark.parametrize("tokens", [1, 5])
+def test_tc_merge_of_many_segments(K, tokens):
+    """One row and one head over 4000 keys: each of the 148 CTAs gets about one tile, so the unit has ~32 segments
+    and the last CTA to finish merges all of them."""
+    d, cap = 128, 4096
+    lengths = torch.tensor([4000 - tokens])
+    kc = randn((1, 1, cap, d), torch.bfloat16, 130)
+    vc = randn((1, 1, cap, d), torch.bfloat16, 131)
+    q = randn((tokens, 1, d), torch.bfloat16, 132)
+    if tokens == 1:
+        out = K.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), cap, d**-0.5)
+        want = oatt.decode_attention(q, kc, vc, lengths, d**-0.5)
+    else:
+        out = K.draft_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), tokens, cap, d**-0.5)
+        want = oatt.draft_attention(q, kc, vc, lengths, tokens, d**-0.5)
+    check_attention(out, want, torch.bfloat16, what=f"many segments T={tokens}")
+    assert _counters_zero(K)
+    assert K.read_status() == 0
+
+
+def test_tc_merge_shapes_in_turn_share_one_workspace(K):
+    """Calls of different shapes in a row reuse the stream's workspace: every result is right and the counters are
+    zero after each."""
+    d, cap = 128, 2048
+    kc = randn((8, 32, cap, d), torch.bfloat16, 140).cuda()
+    vc = randn((8, 32, cap, d), torch.bfloat16, 141).cuda()
+    g = torch.Generator().manual_seed(142)
+    for i, (b, h, tokens) in enumerate(((8, 32, 5), (3, 7, 1), (8, 32, 1), (5, 32, 9), (8, 32, 5))):
+        lengths = torch.randint(0, cap - tokens, (b,), generator=g)
+        q = randn((b * tokens, h, d), torch.bfloat16, 150 + i)
+        if tokens == 1:
+            out = K.decode_attention(q.cuda(), kc[:, :h], vc[:, :h], lengths.cuda(), cap, d**-0.5)
+            want = oatt.decode_attention(q, kc[:, :h].cpu(), vc[:, :h].cpu(), lengths, d**-0.5)
+        else:
+            out = K.draft_attention(q.cuda(), kc[:, :h], vc[:, :h], lengths.cuda(), tokens, cap, d**-0.5)
+            want = oatt.draft_attention(q, kc[:, :h].cpu(), vc[:, :h].cpu(), lengths, tokens, d**-0.5)
+        check_attention(out, want, torch.bfloat16, what=f"call {i}: b={b} h={h} T={tokens}")
+        assert _counters_zero(K), f"counters left non-zero after call {i}"
+    assert K.read_status() == 0
+
+
+def test_tc_merge_writes_every_output_row_through_the_c_abi(K):
+    """Through the C ABI with an output pre-filled with NaN and a freshly zeroed workspace: rows of length 0 get
+    zeros (the pass writes them; no combine runs), every other row its attention."""
+    import ctypes
+
+    from omniasr_b200 import _lib
+
+    lib = _lib.load()
+    b, h, d, cap = 6, 16, 128, 1500
+    lengths = torch.tensor([0, 1400, 0, 7, 129, 1500])
+    kc = randn((b, h, cap, d), torch.bfloat16, 160)
+    vc = randn((b, h, cap, d), torch.bfloat16, 161)
+    q = randn((b, h, d), torch.bfloat16, 162)
+    qd, kd, vd, ld = q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda()
+    out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+    nbytes = lib.omniasr_attention_workspace(_lib.DECODE, _lib.BF16, b, 1, h, d, cap, 0)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    vp = ctypes.c_void_p
+    code = lib.omniasr_decode_attention(vp(qd.data_ptr()), vp(kd.data_ptr()), vp(vd.data_ptr()), b, cap,
+                                        kd.stride(0), kd.stride(1), kd.stride(2), vp(ld.data_ptr()),
+                                        vp(out.data_ptr()), b, h, d, cap, d**-0.5, _lib.BF16, vp(ws.data_ptr()),
+                                        ws.numel(), vp(status.data_ptr()),
+                                        vp(torch.cuda.current_stream().cuda_stream))
+    assert code == 0, lib.omniasr_last_error()
+    torch.cuda.synchronize()
+    assert not torch.isnan(out).any()
+    assert not out[0].any() and not out[2].any()
+    check_attention(out, oatt.decode_attention(q, kc, vc, lengths, d**-0.5), torch.bfloat16, what="c abi")
+    assert not ws[:65536].any() and int(status.item()) == 0
+
+
+def test_tc_shape_past_the_counters_uses_the_combine(K):
+    """More (row, head) units than the workspace has counters for (520 x 32 > 16384): the split units are merged by
+    the combine kernel instead, with the same results."""
+    b, h, d, cap = 520, 32, 128, 128
+    lengths = torch.randint(0, cap + 1, (b,), generator=torch.Generator().manual_seed(170))
+    kc = randn((b, h, cap, d), torch.bfloat16, 171)
+    vc = randn((b, h, cap, d), torch.bfloat16, 172)
+    q = randn((b, h, d), torch.bfloat16, 173)
+    out = K.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), cap, d**-0.5)
+    check_attention(out, oatt.decode_attention(q, kc, vc, lengths, d**-0.5), torch.bfloat16, what="combine path")
+    assert K.read_status() == 0
+
+
 # ------------------------------------------------------------------------------------------------------ prefill
 
 
