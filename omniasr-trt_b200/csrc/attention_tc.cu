@@ -294,6 +294,76 @@ OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int l
   }
 }
 
+// Running merge of segments for JC query columns (lane l holds dims 4l .. 4l+3): max (log2 units), sum, output.
+// The merge is the combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max); a segment that saw no key
+// (sum 0) takes no part, whatever its max.
+template <int JC>
+struct SegAcc {
+  float m[JC], l[JC];
+  float4 o[JC];
+  OMNI_DEV void clear() {
+#pragma unroll
+    for (int c = 0; c < JC; ++c) {
+      m[c] = -INFINITY;
+      l[c] = 0.f;
+      o[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  OMNI_DEV void add(int c, float em, float el, const float4& ev) {
+    if (el > 0.f) {
+      const float mn = fmaxf(m[c], em);
+      const float a = ex2(m[c] - mn), b = ex2(em - mn);
+      o[c] = make_float4(fmaf(o[c].x, a, ev.x * b), fmaf(o[c].y, a, ev.y * b), fmaf(o[c].z, a, ev.z * b),
+                         fmaf(o[c].w, a, ev.w * b));
+      l[c] = fmaf(l[c], a, el * b);
+      m[c] = mn;
+    }
+  }
+};
+
+// Adds the segments of unit (g, h), queries j0 .. j0+JC-1, other than `own`, from the partial arrays (read through
+// L2: other CTAs wrote them). Segments go outermost so that the chunk's loads of one segment are all in flight.
+template <int JC>
+OMNI_DEV void add_other_segments(SegAcc<JC>& acc, const Params& p, int g, int h, int j0, int own, int nseg, int lane) {
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
+#pragma unroll 1
+  for (int s = 0; s < nseg; ++s) {
+    if (s == own) continue;
+    float2 e[JC];
+    float4 v[JC];
+#pragma unroll
+    for (int c = 0; c < JC; ++c) {
+      const int j = j0 + c;
+      if (j < p.nq) {
+        const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
+        e[c] = __ldcg(ml + part);
+        v[c] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * D) + lane);
+      } else {
+        e[c] = make_float2(0.f, 0.f);
+        v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < JC; ++c) acc.add(c, e[c].x, e[c].y, v[c]);
+  }
+}
+
+// Adds this CTA's own segment (its stash) and writes the unit's output rows j0 .. j0+JC-1.
+template <int JC>
+OMNI_DEV void finish_unit(SegAcc<JC>& acc, const Params& p, int g, int h, int j0, int lane, const float* red_l,
+                          const float* stash_m, const float* stash) {
+#pragma unroll
+  for (int c = 0; c < JC; ++c) {
+    const int j = j0 + c;
+    if (j < p.nq) {
+      const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
+      acc.add(c, stash_m[j], l, *reinterpret_cast<const float4*>(stash + j * D + 4 * lane));
+      const int64_t rowh = ((int64_t)g * p.nq + j) * p.heads + h;
+      store_out4(p.out + rowh * D + 4 * lane, acc.o[c], acc.l[c] > 0.f ? 1.f / acc.l[c] : 0.f);
+    }
+  }
+}
+
 // S^T[buf] = K_tile (slot ks) . Q^T  (thread 0).
 OMNI_DEV void issue_scores(uint32_t tbase, int buf, const unsigned char* kslot, const unsigned char* qs) {
   const uint32_t kaddr = smem_addr(kslot);
@@ -726,57 +796,131 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float* red_l = reinterpret_cast<const float*>(smem + L::RED_L_OFF);
     const float* stash_m = reinterpret_cast<const float*>(smem + L::STASH_M_OFF);
     const float* stash = reinterpret_cast<const float*>(smem + L::STASH_OFF);
-    int segs = 0;
-    for (TileIter ti = first_tile; !ti.done; ti.advance()) {
-      if (!ti.last_here()) continue;
-      if (!mbar_wait_or(&seg_ready, segs & 1, &abort_flag)) {
-        abort_flag = 1;
-        break;
-      }
-      const int64_t pos0 = ti.unit_pos0();
-      const int64_t seg0 = pos0 / per;  // the unit's first CTA
-      const int seg = (int)(blockIdx.x - seg0);
-      const int nseg = (int)((pos0 + kTileCost * (ti.tiles - 1)) / per - seg0 + 1);
-      const bool whole = nseg == 1;
-      // In-pass merge of a unit cut between CTAs: the segments are counted per unit; the CTA that finds the others
-      // all published (one acquire load) merges at once from its stash without publishing its own, else it
-      // publishes and counts, and the last to count merges.
-      unsigned* ctr = merge_here && !whole ? p.counters + (int64_t)ti.g * p.heads + ti.h : nullptr;
-      bool last = false;
-      if (ctr) {
-        unsigned c = 0;
-        if (lane == 0) c = ld_acquire_gpu(ctr);
-        last = __shfl_sync(0xffffffffu, c, 0) == (unsigned)(nseg - 1);
-      }
-      if (!last) {
-        for (int j = 0; j < p.nq && j < NQT; ++j) {
-          const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
-          const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
-          const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-          if (whole && p.out) {
-            store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
-          } else {
-            const int64_t part = rowh * p.st + seg;
-            *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
-            if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+    if constexpr (NQT <= 2) {
+      // Decode (one or two queries per unit): while it waits for the stash, this warp watches the unit's counter
+      // (every lane loads it with acquire semantics, one L2 request); once every other CTA of the unit has
+      // counted, this CTA is the unit's last, and the others' segments are merged in registers before the stash
+      // is ready, so that only its own segment and the stores remain (measured: 3 % off the decode step). With
+      // more queries the same code slowed the softmax warps' steady state (the kernel's register allocation
+      // changes), so those keep the plain path below.
+      constexpr int JC = NQT;
+      int segs = 0;
+      for (TileIter ti = first_tile; !ti.done; ti.advance()) {
+        if (!ti.last_here()) continue;
+        const int64_t pos0 = ti.unit_pos0();
+        const int64_t seg0 = pos0 / per;  // the unit's first CTA
+        const int seg = (int)(blockIdx.x - seg0);
+        const int nseg = (int)((pos0 + kTileCost * (ti.tiles - 1)) / per - seg0 + 1);
+        const bool whole = nseg == 1;
+        unsigned* ctr = merge_here && !whole ? p.counters + (int64_t)ti.g * p.heads + ti.h : nullptr;
+        SegAcc<JC> acc;
+        acc.clear();
+        bool last = false;  // this CTA merges the unit
+        // Only the unit's first CTA watches: it works on the unit at the end of its range, the others at the start of
+        // theirs, so it is normally the last. The polls are spaced out (the spinning warp shares its SM sub-partition
+        // with a softmax warp); decisions are taken from lane 0's view, so that the warp stays converged.
+        if (ctr && seg == 0) {
+          const uint64_t t0 = global_ns();
+          while (!__shfl_sync(0xffffffffu, mbar_test_wait(&seg_ready, segs & 1), 0)) {
+            if (__shfl_sync(0xffffffffu, abort_flag != 0 || global_ns() - t0 > kWaitLimitNs, 0)) break;
+            if (__shfl_sync(0xffffffffu, ld_acquire_gpu(ctr), 0) == (unsigned)(nseg - 1)) {
+              add_other_segments<JC>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);
+              last = true;
+              break;
+            }
+            __nanosleep(256);
           }
         }
-        if (ctr) {
-          __threadfence();  // this lane's partial stores before the count
-          __syncwarp();
-          unsigned old = 0;
-          if (lane == 0) old = atomicAdd(ctr, 1u);
-          last = __shfl_sync(0xffffffffu, old, 0) == (unsigned)(nseg - 1);
+        if (!mbar_wait_or(&seg_ready, segs & 1, &abort_flag)) {
+          abort_flag = 1;
+          break;
         }
+        bool counted = false;  // last, found after the stash was ready: the others' segments are still to be read
+        if (ctr && !last) counted = last = __shfl_sync(0xffffffffu, ld_acquire_gpu(ctr), 0) == (unsigned)(nseg - 1);
+        if (!last) {
+          for (int j = 0; j < p.nq && j < NQT; ++j) {
+            const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
+            const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
+            const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
+            if (whole && p.out) {
+              store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
+            } else {
+              const int64_t part = rowh * p.st + seg;
+              *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
+              if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+            }
+          }
+          if (ctr) {
+            __threadfence();  // this lane's partial stores before the count
+            __syncwarp();
+            unsigned old = 0;
+            if (lane == 0) old = atomicAdd(ctr, 1u);
+            counted = last = __shfl_sync(0xffffffffu, old, 0) == (unsigned)(nseg - 1);
+            if (last) __threadfence();  // the other CTAs' partials after their counts
+          }
+        }
+        if (last) {
+          if (counted) add_other_segments<JC>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);  // else merged while waiting
+          finish_unit<JC>(acc, p, ti.g, ti.h, 0, lane, red_l, stash_m, stash);
+          if (lane == 0) *ctr = 0;  // zero again for the next call
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&seg_free);
+        ++segs;
       }
-      if (last) {
-        __threadfence();  // the other CTAs' partials after their counts
-        merge_unit<NQT>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
-        if (lane == 0) *ctr = 0;  // zero again for the next call
+    } else {
+      int segs = 0;
+      for (TileIter ti = first_tile; !ti.done; ti.advance()) {
+        if (!ti.last_here()) continue;
+        if (!mbar_wait_or(&seg_ready, segs & 1, &abort_flag)) {
+          abort_flag = 1;
+          break;
+        }
+        const int64_t pos0 = ti.unit_pos0();
+        const int64_t seg0 = pos0 / per;  // the unit's first CTA
+        const int seg = (int)(blockIdx.x - seg0);
+        const int nseg = (int)((pos0 + kTileCost * (ti.tiles - 1)) / per - seg0 + 1);
+        const bool whole = nseg == 1;
+        // In-pass merge of a unit cut between CTAs: the segments are counted per unit; the CTA that finds the others
+        // all published (one acquire load) merges at once from its stash without publishing its own, else it
+        // publishes and counts, and the last to count merges.
+        unsigned* ctr = merge_here && !whole ? p.counters + (int64_t)ti.g * p.heads + ti.h : nullptr;
+        bool last = false;
+        if (ctr) {
+          unsigned c = 0;
+          if (lane == 0) c = ld_acquire_gpu(ctr);
+          last = __shfl_sync(0xffffffffu, c, 0) == (unsigned)(nseg - 1);
+        }
+        if (!last) {
+          for (int j = 0; j < p.nq && j < NQT; ++j) {
+            const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
+            const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
+            const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
+            if (whole && p.out) {
+              store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
+            } else {
+              const int64_t part = rowh * p.st + seg;
+              *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
+              if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+            }
+          }
+          if (ctr) {
+            __threadfence();  // this lane's partial stores before the count
+            __syncwarp();
+            unsigned old = 0;
+            if (lane == 0) old = atomicAdd(ctr, 1u);
+            last = __shfl_sync(0xffffffffu, old, 0) == (unsigned)(nseg - 1);
+          }
+        }
+        if (last) {
+          __threadfence();  // the other CTAs' partials after their counts
+          merge_unit<NQT>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
+          if (lane == 0) *ctr = 0;  // zero again for the next call
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&seg_free);
+        ++segs;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&seg_free);
-      ++segs;
     }
   }
   __syncthreads();
