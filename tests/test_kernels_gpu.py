@@ -331,6 +331,33 @@ def test_beam_attention_graded_shape(K):
     check_attention(out, want, torch.bfloat16, what="config 3")
 
 
+@pytest.mark.parametrize("s,n,gcap", [(64, 4, 40), (3, 9, 17)])
+def test_beam_attention_many_items_and_empty_rows(K, s, n, gcap):
+    """The beam combine's warps each take many (row, head) items (64 inputs x 4 beams x 32 heads), or nine beams per
+    input (the 16-query pass); an input without context and rows without generated keys (one row with neither:
+    zeros)."""
+    h, d, cap = 32, 128, 1100
+    r = s * n
+    g = torch.Generator().manual_seed(180 + n)
+    ctx_len = torch.randint(1, cap + 1, (s,), generator=g)
+    ctx_len[1] = 0
+    gen_len = torch.randint(0, gcap + 1, (r,), generator=g)
+    gen_len[n] = 0  # input 1's first beam: no context, no generated keys
+    gen_len[0] = 0
+    kc = randn((s, h, cap, d), torch.bfloat16, 181)
+    vc = randn((s, h, cap, d), torch.bfloat16, 182)
+    kg = randn((r, h, gcap, d), torch.bfloat16, 183)
+    vg = randn((r, h, gcap, d), torch.bfloat16, 184)
+    q = randn((r, h, d), torch.bfloat16, 185)
+    ptr = (torch.arange(r)[:, None] // n * n + torch.randint(0, n, (r, gcap), generator=g)).to(torch.int32)
+    out = K.beam_attention(q.cuda(), kc.cuda(), vc.cuda(), ctx_len.cuda(), kg.cuda(), vg.cuda(), ptr.cuda(),
+                           gen_len.cuda(), n, cap, d**-0.5)
+    want = oatt.beam_attention(q, kc, vc, ctx_len, kg, vg, ptr, gen_len, n, d**-0.5)
+    check_attention(out, want, torch.bfloat16, what=f"beam s={s} n={n}")
+    assert not out[n].any()
+    assert K.read_status() == 0
+
+
 def test_beam_pointer_out_of_range_is_flagged(K):
     s, n, h, d, cap, gcap = 1, 2, 1, 128, 64, 8
     kc = torch.zeros(s, h, cap, d, device="cuda")
