@@ -1149,16 +1149,17 @@ int tc_prefetch() {
   return n < 0 ? 0 : n;
 }
 
-// Cost of a unit's start and epilogue in tile-eighths. Measured on B200 (config-2 and config-1 shapes): units of
-// several query rows split best at one tile (8), single-query units at 0 -- their epilogue is short, and a finer
-// split evens out the CTAs' ends. OMNIASR_TC_UNIT_COST overrides both.
+// Cost of a unit's start and epilogue in tile-eighths. Measured on B200 (config-2 and config-1 shapes, with the
+// in-pass merge): units of several query rows split best at 10 (0.7 % faster than 8 on the verify step; 4-16
+// swept), single-query units at 0 -- their epilogue is short, and a finer split evens out the CTAs' ends.
+// OMNIASR_TC_UNIT_COST overrides both.
 int tc_unit_cost(int nq) {
   static const int c = [] {
     const char* e = getenv("OMNIASR_TC_UNIT_COST");
     return e ? atoi(e) : -1;
   }();
   if (c >= 0) return c;
-  return nq <= 1 ? 0 : 8;
+  return nq <= 1 ? 0 : 10;
 }
 
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
