@@ -114,13 +114,25 @@ struct TileIter {
     pos = pre + h * ucost + p->unit_cost + kTileCost * t;
     if (pos >= c1) done = true;
   }
-  OMNI_DEV void init(const Params& pp, int64_t c0, int64_t c1_) {
+  // pre_tab (optional): pre_tab[g] = cost of the groups before g, for g <= groups (a binary search instead of a
+  // walk over the groups).
+  OMNI_DEV void init(const Params& pp, int64_t c0, int64_t c1_, const int64_t* pre_tab = nullptr) {
     p = &pp;
     c1 = c1_;
     g = 0;
     pre = 0;
     h = t = 0;
     done = false;
+    if (pre_tab) {
+      int lo = 0, hi = p->groups - 1;  // the first group that ends past c0 (else the last)
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (pre_tab[mid + 1] > c0) hi = mid;
+        else lo = mid + 1;
+      }
+      g = lo;
+      pre = pre_tab[g];
+    }
     load_group();
     while (g < p->groups - 1 && c0 >= pre + ucost * p->heads) {
       pre += ucost * p->heads;
@@ -455,13 +467,36 @@ __global__ void __launch_bounds__(THREADS, 1)
   // The queries, the cache rows and the lengths may come from the kernel before this one.
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // The lengths, read by every role's walk, once into shared memory.
+  // The lengths, read by every role's walk, once into shared memory, with the groups' cost prefix (thread g
+  // computes group g's cost; a block-wide scan sums them).
+  static_assert(kSmemGroups <= THREADS, "one thread per group for the cost prefix");
   __shared__ int64_t s_len[kSmemGroups];
+  __shared__ int64_t s_pre[kSmemGroups + 1];
+  __shared__ int64_t s_wsum[THREADS / 32];
   Params p = pin;
+  const int64_t* pre_tab = nullptr;
   if (p.groups <= kSmemGroups) {
-    for (int g = tid; g < p.groups; g += THREADS) s_len[g] = pin.lengths[g];
+    int64_t c = 0;
+    if (tid < p.groups) {
+      const int64_t len = pin.lengths[tid];
+      s_len[tid] = len;
+      int64_t n = len + (p.causal ? p.nq - 1 : 0);
+      n = n < 0 ? 0 : (n > p.cap ? p.cap : n);
+      c = unit_cost(p, (n + BN - 1) / BN) * p.heads;
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, c, off);
+      if (lane >= off) c += y;
+    }
+    if (lane == 31) s_wsum[warp] = c;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) c += s_wsum[w];
+    if (tid < p.groups) s_pre[tid + 1] = c;
+    if (tid == 0) s_pre[0] = 0;
     __syncthreads();
     p.lengths = s_len;
+    pre_tab = s_pre;
   }
   if (tid == 0) OMNI_TRACE_AT(4003);
   const bool merge_here = p.counters != nullptr && p.out != nullptr;  // no combine kernel follows
@@ -483,14 +518,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
-  const int64_t total = total_cost(p);
+  const int64_t total = pre_tab ? pre_tab[p.groups] : total_cost(p);
   if (tid == 0) OMNI_TRACE_AT(4007);
   // At least one tile's cost per CTA, so that every CTA between a unit's first and last owns one of its tiles.
   const int64_t per = max((total + gridDim.x - 1) / gridDim.x, kTileCost);
   const int64_t c0 = (int64_t)blockIdx.x * per;
   const int64_t c1 = min(total, c0 + per);
   TileIter first_tile;  // this CTA's first tile; every role starts its walk from a copy
-  first_tile.init(p, c0, c1);
+  first_tile.init(p, c0, c1, pre_tab);
   const bool has_work = c0 < c1 && !first_tile.done;  // uniform over the CTA
   if (tid == 0) OMNI_TRACE_AT(4008);
   OMNI_TRACE_CTA(0);
