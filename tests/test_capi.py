@@ -71,6 +71,22 @@ def test_workspace_sizes():
     assert lib.omniasr_attention_workspace(_lib.DECODE, 7, 8, 1, 32, 128, 2048, 0) == 0
 
 
+def test_decode_and_draft_workspaces_start_with_the_unit_counters():
+    """ABI version 2: decode / draft workspaces hold OMNIASR_ATTENTION_COUNTER_BYTES (64 KB) of per-(row, head)
+    counters before the split partials, on the tensor-core path (bf16, head_dim 128) and the CUDA-core path alike."""
+    lib = _lib.load()
+    counters = 65536
+    header = (ROOT / "include" / "omniasr_b200.h").read_text()
+    assert f"#define OMNIASR_ATTENTION_COUNTER_BYTES {counters}" in header
+    for kind, per in ((_lib.DECODE, 1), (_lib.DRAFT, 5)):
+        for dtype, dim in ((_lib.BF16, 128), (_lib.F32, 128), (_lib.BF16, 64)):
+            n = lib.omniasr_attention_workspace(kind, dtype, 8, per, 32, dim, 2048, 0)
+            assert n >= counters + 8 * per * 32 * (dim + 2) * 4, (kind, dtype, dim, n)
+    # The beam workspace carries no counters: one split of partials per (row, head) suffices for a tiny shape.
+    n = lib.omniasr_attention_workspace(_lib.BEAM, _lib.BF16, 1, 1, 1, 128, 128, 0)
+    assert 0 < n < counters
+
+
 def test_no_device_is_an_error_not_a_fallback():
     """Without a GPU the compute entry points return an error code (no CPU path behind them)."""
     import torch
