@@ -528,6 +528,26 @@ def test_tc_merge_writes_every_output_row_through_the_c_abi(K):
     assert not ws[:65536].any() and int(status.item()) == 0
 
 
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_tc_merge_with_more_rows_than_the_shared_length_table(K, tokens):
+    """300 rows x 32 heads: more rows than the pass keeps in shared memory (256; the schedule then walks the lengths
+    in global memory) but within the unit counters, so split units are still merged inside the pass."""
+    b, h, d, cap = 300, 32, 128, 384
+    lengths = torch.randint(0, cap - tokens + 1, (b,), generator=torch.Generator().manual_seed(175 + tokens))
+    kc = randn((b, h, cap, d), torch.bfloat16, 176)
+    vc = randn((b, h, cap, d), torch.bfloat16, 177)
+    q = randn((b * tokens, h, d), torch.bfloat16, 178)
+    if tokens == 1:
+        out = K.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), cap, d**-0.5)
+        want = oatt.decode_attention(q, kc, vc, lengths, d**-0.5)
+    else:
+        out = K.draft_attention(q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda(), tokens, cap, d**-0.5)
+        want = oatt.draft_attention(q, kc, vc, lengths, tokens, d**-0.5)
+    check_attention(out, want, torch.bfloat16, what=f"300 rows T={tokens}")
+    assert _counters_zero(K)
+    assert K.read_status() == 0
+
+
 def test_tc_shape_past_the_counters_uses_the_combine(K):
     """More (row, head) units than the workspace has counters for (520 x 32 > 16384): the split units are merged by
     the combine kernel instead, with the same results."""
