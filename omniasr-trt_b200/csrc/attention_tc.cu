@@ -4,7 +4,9 @@
 // Schedule (persistent, stream-K): the keys of every (group, head) unit are cut into 128-key tiles; the grid is
 // one CTA per SM and CTA b takes the contiguous tile range [b * per, (b + 1) * per) of the concatenated units, so
 // every SM streams the same number of K/V bytes whatever the ragged lengths. A unit cut between CTAs leaves one
-// partial (max, sum, unnormalised output) per CTA ("segment"); the combine kernel merges the segments of a unit.
+// partial (max, sum, unnormalised output) per CTA ("segment"). For decode and draft calls the last CTA to finish a
+// unit merges its segments itself (a per-unit counter at the head of the workspace says which CTA is last); for
+// beam search, whose generated keys are attended separately, a combine kernel merges them.
 //
 // One CTA (256 threads): warp 4 loads the queries and the K tiles, warp 6 the V tiles (TMA, two 64-column boxes
 // each, 128-byte swizzle, three 32 KB slots per operand); warp 5 issues the MMAs; warps 0-3 run the softmax,
