@@ -2,9 +2,10 @@
 
 The reference package (Wataru-Nakata/omniasr-trt, pure Python) is imported from ``baseline/_ref`` where it is
 installed next to this repository; ``omniasr_b200.dropin.install()`` swaps its ``omniasr_trt.kernels``. These
-restate the reference's CUDA integration tests (tests/test_kernels.py:58-95, :129-150; tests/test_spec.py:111-130)
+restate the reference's CUDA integration tests (tests/test_kernels.py:58-95, :129-150; tests/test_spec.py:111-198)
 with the same small random model (tests/test_decode.py:17-28): token sequences must be identical to the unfused
-PyTorch step and to the reference-order loops.
+PyTorch step, to the greedy search and to the reference-order loops, and LLMTranscriber.transcribe must give the
+reference-order transcripts.
 """
 
 import sys
@@ -109,3 +110,122 @@ def test_speculative_decoder_same_tokens_as_greedy(ref):
     dec.drafts = lambda j: (want[j] + [5, 6, 7], 0)  # perfect drafts: several tokens per step
     assert dec.generate(ctxs) == want
     assert dec.stats["tokens"] / dec.stats["rows_steps"] > 1.5
+
+
+# --- speculative decoding on these kernels (propose / accept, RoPE + append, verify attention): whatever the drafts,
+# the tokens are the greedy search's. The scenarios (model seeds, context lengths, random draws) are those of the
+# reference's own tests/test_spec.py:111-198, which pin the same behaviour on its Triton kernels.
+
+def _corrupt(tokens, rng, vocab=12):
+    """A draft that drifts from the tokens: some replaced, some dropped, some doubled with a stray token, and five
+    random tokens at the end."""
+    out = []
+    for tok in tokens:
+        u = rng.random()
+        if u < 0.1:
+            out.append(int(rng.integers(3, vocab)))
+        elif u < 0.15:
+            pass
+        elif u < 0.2:
+            out.extend([tok, int(rng.integers(3, vocab))])
+        else:
+            out.append(tok)
+    return out + [int(x) for x in rng.integers(3, vocab, 5)]
+
+
+def _spec_run(dec, ctxs, drafts):
+    dec.drafts = lambda j: drafts[j]
+    return dec.generate(ctxs)
+
+
+@pytest.mark.parametrize("draft_tokens", [1, 4, 8])
+def test_speculative_decoder_any_draft(ref, draft_tokens):
+    import numpy as np
+
+    m = small_model(ref["modeling"], seed=21)
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    torch.manual_seed(22)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (40, 7, 251, 90, 13, 60)]
+    want = [t.greedy_reference(c) for c in ctxs]
+    assert min(len(w) for w in want) >= 3
+    rng = np.random.default_rng(0)
+    dec = ref["spec"].SpecDecoder(m, draft_tokens=draft_tokens, max_batch=4, sync_every=3, reserve=8)
+    assert _spec_run(dec, ctxs, [(w + [5, 6, 7], 0) for w in want]) == want  # right, and running on past EOS
+    per_step = dec.stats["tokens"] / dec.stats["rows_steps"]
+    assert _spec_run(dec, ctxs, [(_corrupt(w, rng), 0) for w in want]) == want
+    assert _spec_run(dec, ctxs, [(_corrupt(w[3:], rng), 2) for w in want]) == want  # the draft starts later
+    others = [[int(x) for x in rng.integers(3, 12, 30)] for _ in ctxs[2:]]
+    assert _spec_run(dec, ctxs, [None, ([], 0)] + [(o, 0) for o in others]) == want  # none, empty, unrelated
+    if draft_tokens > 1:
+        assert per_step > 1.5  # right drafts: several tokens per step
+
+
+def test_speculative_decoder_eos_and_limit_inside_a_step(ref, monkeypatch):
+    """Rows that reach EOS or the position limit in the middle of a drafted step stop there, as the greedy search."""
+    m = small_model(ref["modeling"], seed=23)
+    with torch.no_grad():
+        m.final_proj.weight[ref["llm"].EOS] *= 0.3  # long generations
+    monkeypatch.setattr(ref["decode"], "LIMIT", 70)
+    monkeypatch.setattr(ref["spec"], "LIMIT", 70)
+    torch.manual_seed(24)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (5, 30, 64, 69, 12)]
+    want = ref["decode"].GreedyDecoder(m, max_batch=3, sync_every=4, reserve=8).generate(ctxs)
+    dec = ref["spec"].SpecDecoder(m, draft_tokens=6, max_batch=3, sync_every=4, reserve=8)
+    assert _spec_run(dec, ctxs, [(w + [4] * 20, 0) for w in want]) == want
+
+
+def test_speculative_decoder_repetition_stop(ref):
+    """Without EOS a row ends by the repetition stop, and the cache grows meanwhile."""
+    import numpy as np
+
+    m = small_model(ref["modeling"], seed=15)
+    with torch.no_grad():
+        m.final_proj.weight[ref["llm"].EOS] = 0.0
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    torch.manual_seed(25)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (5, 60, 140, 151)]
+    want = [t.greedy_reference(c) for c in ctxs]
+    rng = np.random.default_rng(3)
+    dec = ref["spec"].SpecDecoder(m, draft_tokens=4, max_batch=3, sync_every=5, reserve=8)
+    dec.context_floor = 0
+    assert _spec_run(dec, ctxs, [(_corrupt(w, rng), 0) for w in want]) == want
+    assert dec.stats["grows"] >= 1
+
+
+def test_speculative_decoder_own_tokens(ref):
+    """No draft: the proposals come from the row's own repeating tokens (several tokens per step)."""
+    m = small_model(ref["modeling"], seed=15)
+    with torch.no_grad():
+        m.final_proj.weight[ref["llm"].EOS] = 0.0
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    torch.manual_seed(26)
+    ctxs = [torch.randn(n, 32, device="cuda") for n in (5, 60, 99)]
+    want = [t.greedy_reference(c) for c in ctxs]
+    dec = ref["spec"].SpecDecoder(m, draft_tokens=4, max_batch=3, sync_every=5, reserve=8)
+    assert _spec_run(dec, ctxs, [None] * len(ctxs)) == want
+    assert dec.stats["tokens"] / dec.stats["rows_steps"] > 1.5
+
+
+def test_transcriber_on_these_kernels(ref):
+    """LLMTranscriber.transcribe end to end (segmentation, context building, prefill, decoding) with frame drafts,
+    partial drafts, own tokens and one token per step gives the reference-order transcripts."""
+    import numpy as np
+
+    llm = ref["llm"]
+    m = small_model(ref["modeling"], seed=3)
+    t = llm.LLMTranscriber(m, FakeTokenizer(), max_batch=3)
+    rng = np.random.default_rng(0)
+    old = llm.SEGMENT
+    llm.SEGMENT = 2000
+    try:
+        waves = [rng.standard_normal(n).astype(np.float32) for n in (5000, 2000, 900)]
+        langs = ["aae_Latn", None, "AAL_latn"]
+        want = t.transcribe(waves, langs, mode="reference")
+        frames = [rng.integers(0, 12, n // 320) for n in (5000, 2000, 900)]
+        assert t.transcribe(waves, langs, drafts=frames) == want
+        assert t.transcribe(waves, langs, drafts=[None, frames[1], None]) == want
+        assert t.transcribe(waves, langs) == want
+        t.draft_tokens = 0  # one token per step
+        assert t.transcribe(waves, langs) == want
+    finally:
+        llm.SEGMENT = old
