@@ -229,3 +229,32 @@ def test_transcriber_on_these_kernels(ref):
         assert t.transcribe(waves, langs) == want
     finally:
         llm.SEGMENT = old
+
+
+def test_public_api_on_these_kernels(ref):
+    """The reference's public surface on these kernels: OmniASRLLM.transcribe and compat.Pipeline.transcribe (the
+    omnilingual-asr look-alike: dict inputs, 16 kHz, greedy or beam search by its config) give the reference-order
+    transcripts."""
+    import numpy as np
+
+    llm = ref["llm"]
+    import omniasr_trt
+    from omniasr_trt import compat
+
+    m = small_model(ref["modeling"], seed=40)
+    t = llm.LLMTranscriber(m, FakeTokenizer(), max_batch=2)
+    rng = np.random.default_rng(41)
+    old = llm.SEGMENT
+    llm.SEGMENT = 2000
+    try:
+        waves = [rng.standard_normal(n).astype(np.float32) for n in (4100, 900, 2600)]
+        langs = [None, "aae_Latn", None]
+        greedy = t.transcribe(waves, langs, mode="reference")
+        beam3 = t.transcribe(waves, langs, mode="reference", beams=3)
+        model = omniasr_trt.OmniASRLLM(t)
+        assert model.transcribe(waves, langs) == greedy
+        inputs = [{"waveform": w, "sample_rate": 16000} for w in waves]
+        assert compat.Pipeline(model).transcribe(inputs, lang=langs) == greedy
+        assert compat.Pipeline(model, {"nbest": 3}).transcribe(inputs, lang=langs) == beam3
+    finally:
+        llm.SEGMENT = old
