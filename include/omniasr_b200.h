@@ -184,11 +184,14 @@ int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w
  * omniasr_decode_attention() minus the workspace, which here is a device array inside this library of
  * omniasr_noalloc_scratch_bytes() bytes (8 MiB), held on every GPU that loads the library until the process
  * exits. For a host whose device memory is owned by another allocator, or a plugin interface that hands over
- * only the input and output buffers. Shapes whose split partials exceed the array are rejected with
- * OMNIASR_ERR_WORKSPACE. The first call on a device looks up the array's address (cudaGetSymbolAddress) and
- * should come before any stream capture. All calls on a device share the array: calls whose kernels overlap on
- * the GPU race, so order them (same stream, or events). The array's leading unit counters start at zero (a
- * static device array is zero-initialised when the library loads) and every call leaves them zero. */
+ * only the input and output buffers. Arguments are checked as by omniasr_decode_attention(); shapes whose split
+ * partials exceed the array are then rejected with OMNIASR_ERR_WORKSPACE. The first call on a device (and again
+ * after the device's context is recreated, e.g. by cudaDeviceReset) looks up the array's address with
+ * cudaGetSymbolAddress and should come before any stream capture. All calls on a device share the array: calls
+ * whose kernels overlap on the GPU race, so order them (same stream, or events). The array's leading unit
+ * counters start at zero (a static device array is zero-initialised when the library loads) and every call that
+ * completes normally leaves them zero; after a call that raised status bit 2 (a bounded wait gave up) they may
+ * not be, so call omniasr_noalloc_reset() on the stream before the next no-alloc call. */
 int omniasr_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
                                      int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
                                      const int64_t* lengths, void* out, int batch, int heads, int dim, int keys,
@@ -196,6 +199,17 @@ int omniasr_decode_attention_noalloc(const void* q, const void* k_cache, const v
 
 /* Size in bytes of the device scratch array behind omniasr_decode_attention_noalloc(). */
 size_t omniasr_noalloc_scratch_bytes(void);
+
+/* Zeroes the unit counters at the head of the current device's no-alloc scratch array, in stream order
+ * (cudaMemsetAsync on the array itself; nothing is allocated). Needed only after a no-alloc call raised status
+ * bit 2. No counterpart in the reference. */
+int omniasr_noalloc_reset(cudaStream_t stream);
+
+/* Self-test of the bounded device wait every kernel here uses (no counterpart in the reference): one kernel waits
+ * on an mbarrier that nothing completes, gives up after limit_ns (0 < limit_ns <= 1e8), ORs the timeout bit (2)
+ * into *status and returns; *waited_ns (may be NULL; device memory) gets the time it waited. The context stays
+ * usable. */
+int omniasr_selftest_wait_timeout(int64_t limit_ns, int* status, unsigned long long* waited_ns, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -170,11 +170,15 @@ int omniasr_rope_kv(const void* qkv, int64_t qkv_stride, const float* cs, int64_
   return cuda_status(omni::launch_rope_kv(dtype, dim, a, n, stream), "rope_kv launch");
 }
 
-static int group_attention(const char* name, const void* q, const void* k_cache, const void* v_cache,
-                           int64_t cache_rows, int64_t cache_len, int64_t stride_row, int64_t stride_head,
-                           int64_t stride_pos, const int64_t* lengths, void* out, int groups, int nq, int causal,
-                           int heads, int dim, int keys, float scale, int dtype, void* workspace,
-                           size_t workspace_bytes, int* status, cudaStream_t stream) {
+}  // extern "C"
+
+namespace omni {
+// The argument checks of a decode / draft call, everything but the workspace: OMNIASR_OK or the error code (with
+// the message set). groups == 0 passes (nothing to launch).
+int check_group_args(const char* name, const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                     int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                     const int64_t* lengths, const void* out, int groups, int nq, int heads, int dim, int keys,
+                     int dtype) {
   if (int e = check_common(dtype, dim, heads)) return e;
   if (groups < 0 || nq <= 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: batch %d tokens %d", name, groups, nq);
   if (groups == 0) return ok();
@@ -187,6 +191,21 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
                                        (long long)cache_rows);
   if (keys < 0 || keys > cache_len)
     return fail(OMNIASR_ERR_ARGUMENT, "%s: keys %d outside [0, cache length %lld]", name, keys, (long long)cache_len);
+  return OMNIASR_OK;
+}
+}  // namespace omni
+
+extern "C" {
+
+static int group_attention(const char* name, const void* q, const void* k_cache, const void* v_cache,
+                           int64_t cache_rows, int64_t cache_len, int64_t stride_row, int64_t stride_head,
+                           int64_t stride_pos, const int64_t* lengths, void* out, int groups, int nq, int causal,
+                           int heads, int dim, int keys, float scale, int dtype, void* workspace,
+                           size_t workspace_bytes, int* status, cudaStream_t stream) {
+  if (int e = omni::check_group_args(name, q, k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                                     stride_pos, lengths, out, groups, nq, heads, dim, keys, dtype))
+    return e;
+  if (groups == 0) return ok();
   const int64_t rows_q = (int64_t)groups * nq;
   if (omni::tc_path_enabled(dtype, dim, nq)) {
     const size_t need = omni::kCounterBytes + omni::partial_bytes(rows_q, heads, omni::tc_segments(keys), dim);

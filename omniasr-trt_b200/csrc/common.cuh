@@ -79,12 +79,13 @@ OMNI_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase of `parity` to complete; false after kWaitLimitNs.
-OMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase of `parity` to complete; false after `limit_ns` (kWaitLimitNs unless a self-test asks for
+// a shorter limit).
+OMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
   return true;
 }

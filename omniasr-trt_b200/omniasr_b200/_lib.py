@@ -43,6 +43,8 @@ SIGNATURES = {
     "omniasr_decode_attention_noalloc": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _i, _i, _f,
                                               _i, _p, _p]),
     "omniasr_noalloc_scratch_bytes": (_sz, []),
+    "omniasr_noalloc_reset": (_i, [_p]),
+    "omniasr_selftest_wait_timeout": (_i, [_i64, _p, _p, _p]),
     "omniasr_propose": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _i,
                              _i, _p, _p]),
     "omniasr_accept": (_i, [_p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i, _i, _i64, _i64, _p, _p]),
