@@ -99,6 +99,11 @@ class Workload:
     roof_kernel = ""
     traffic_key = ""
     calls_per_layer = 1
+    # How the roofline call's duration is taken: "whole" -- a step is nothing but the dominant calls, so one call is
+    # the event-free step time / layers; "difference" -- the step minus the same step without the dominant calls
+    # (both event-free graphs); "events" -- CUDA events around each dominant call in a second graph.
+    roof_timing = "whole"
+    skip_dominant = False  # set while capturing the step without its dominant calls ("difference")
 
     def __init__(self, device: torch.device, rank: int, world: int, layers: int):
         from omniasr_b200 import kernels
@@ -137,6 +142,7 @@ class Verify(Workload):
     traffic_key = "draft_attention_config2_bytes_per_call"
     B, T, CAP = 8, 5, 4096
     calls_per_layer = 2  # rope_kv, attention pass (it merges split units itself)
+    roof_timing = "difference"
 
     @classmethod
     def lengths(cls) -> torch.Tensor:
@@ -179,6 +185,8 @@ class Verify(Workload):
 
     def layer(self, i, ev=None):
         q = self.K.rope_kv(self.qkv[i], self.cs, self.pos, self.kc[i], self.vc[i], H, self.slots)
+        if self.skip_dominant:
+            return [q]
         if ev:
             ev[0].record()
         o = self.K.draft_attention(q, self.kc[i], self.vc[i], self.att_len, self.T, self.keys, D**-0.5)
@@ -476,6 +484,7 @@ class Sweep(Workload):
     """64 rows sharded over the ranks; q_len 1 and 5 at lengths 512, 2048 and 8192."""
 
     name = "sweep"
+    roof_timing = "events"  # the roofline call is the largest case (q5, 8192 keys, ~1 ms): events cost nothing there
     metric = "decode-attn HBM GB/s, whole box (64 rows sharded, q_len 1/5, lengths 512/2048/8192)"
     roof_kernel = "draft_attention (q_len 5, 8192 keys)"
     traffic_key = "draft_attention_config5_bytes_per_call"
@@ -546,6 +555,7 @@ class Gemm(Workload):
     QKV, the output projection + residual, gate/inner + SwiGLU, the FFN output + residual (kernels.decode_gemm)."""
 
     name = "gemm"
+    roof_timing = "events"
     metric = "decode GEMM weight-streaming GB/s (QKV, out+res, SwiGLU, FFN-out+res; 40 tokens; 12 layers)"
     roof_kernel = "decode_gemm (QKV: 12288 x 4096)"
     traffic_key = "decode_gemm_qkv_bytes_per_call"
@@ -611,6 +621,65 @@ class Gemm(Workload):
 
 
 WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm)}
+
+
+# ------------------------------------------------------------------------------- the reference's own GPU kernels
+
+
+def reference_gpu_kernels():
+    """The reference's own GPU path for these workloads, unmodified: its Triton kernels (``omniasr_trt.kernels``:
+    rope_kv, decode_attention, draft_attention, beam_attention, kernels.py:294-423) from baseline/_ref, torch's SDPA
+    for the prefill exactly as decode.py:171 calls it, and ``index_select`` for the K/V reorder (llm.py:237-238).
+    Returns (namespace, None) or (None, why not)."""
+    import types
+
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "omniasr_trt" / "kernels.py").exists():
+        return None, "the reference package is not in baseline/_ref"
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        from omniasr_trt import kernels as rk
+    except Exception as e:  # noqa: BLE001
+        return None, f"importing the reference's kernels failed: {e!r}"
+    if getattr(rk, "__omniasr_b200__", False):
+        return None, "the reference's kernel module was replaced in this process"
+    if not rk.available(torch.device("cuda")):
+        return None, "the reference's Triton kernels are not available on this device"
+
+    def prefill_attention(q, k, v, scale=None):
+        return torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale)
+
+    def reorder_gather(src, parent, out=None):
+        return torch.index_select(src, 0, parent, out=out)
+
+    ns = types.SimpleNamespace(rope_kv=rk.rope_kv, decode_attention=rk.decode_attention,
+                               draft_attention=rk.draft_attention, beam_attention=rk.beam_attention,
+                               prefill_attention=prefill_attention, reorder_gather=reorder_gather)
+    return ns, None
+
+
+def graph_ms(side: torch.cuda.Stream, device, fn, steps: int, warmup: int) -> float:
+    """Captures ``fn`` (warmed up once outside the capture) in a CUDA graph on ``side`` and returns the mean replay
+    time in ms over ``steps`` replays after ``warmup``, timed with CUDA events, no events inside the graph."""
+    with torch.cuda.stream(side):
+        fn()
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        g.capture_begin()
+        fn()
+        g.capture_end()
+    torch.cuda.synchronize(device)
+    for _ in range(warmup):
+        g.replay()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(steps):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize(device)
+    return s.elapsed_time(e) / steps
 
 
 # --------------------------------------------------------------------------------------------------------- timing
@@ -732,8 +801,38 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         torch.cuda.synchronize(device)
         per_call.append([a.elapsed_time(b) for a, b in ev])
     per_call = list(np.median(np.array(per_call), axis=0))  # per dominant call, median of 3 replays
-    roof_ms = max_over_ranks(float(np.mean(per_call)) if args.workload != "sweep" else per_call[-1])
+    isolated_ms = max_over_ranks(float(np.mean(per_call)) if args.workload != "sweep" else per_call[-1])
     case_ms = [max_over_ranks(x) for x in per_call] if args.workload == "sweep" else None
+    # The roofline call's duration inside the event-free step, so that layers x per call <= ms_per_step.
+    if wl.roof_timing == "whole":
+        roof_ms = max_over_ranks(ms / args.steps / wl.layers)
+    elif wl.roof_timing == "difference":
+        wl.skip_dominant = True
+        minus_ms = graph_ms(side, device, wl.run, args.steps, args.warmup)
+        wl.skip_dominant = False
+        roof_ms = max_over_ranks((ms / args.steps - minus_ms) / wl.layers)
+    else:
+        roof_ms = isolated_ms
+    roof_how = {"whole": "event-free step time / layers (a step is only the dominant calls)",
+                "difference": "(event-free step - the same step without the dominant calls) / layers",
+                "events": "CUDA events around each dominant call, in a second graph replayed after the timed region "
+                          "(median of 3)"}[wl.roof_timing]
+
+    # The reference's own GPU kernels (Triton; SDPA / index_select where it calls torch) on the same workload, the
+    # same graph timing; the same inputs (the appended rows are rewritten with identical values).
+    gpu_ref = None
+    if hasattr(wl, "run_library"):
+        gpu_ref_why = "this workload's library comparison is cuBLAS (library_baseline)"
+    else:
+        ref_ns, gpu_ref_why = reference_gpu_kernels()
+        if ref_ns is not None:
+            ours = wl.K
+            wl.K = ref_ns
+            try:
+                ref_ms = max_over_ranks(graph_ms(side, device, wl.run, args.steps, args.warmup))
+            finally:
+                wl.K = ours
+            gpu_ref = {"ms_per_step": ref_ms}
 
     # --- end to end through the public API: inputs from pinned host memory, results back, every step ---
     # One graph per step: layer i's inputs are copied in on an input copy stream, its launches run on the capture
@@ -816,16 +915,26 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": peak,
                      "unit": "TFLOP/s" if wl.bound == "tensor" else "GB/s", "frac": round(achieved / peak, 3),
                      "peak_kind": pk["kind"], "kernel": wl.roof_kernel, "traffic": traffic_per_launch(wl.traffic_key),
-                     "timing": "CUDA events around each dominant call, in a second graph replayed after the timed "
-                               "region (median of 3; the events cut the programmatic-launch overlap, so this is "
-                               "conservative)",
+                     "timing": roof_how,
                      ("flops_per_launch" if wl.bound == "tensor" else "bytes_per_launch"): wl.roof_units,
-                     "us_per_launch": round(roof_ms * 1e3, 2)},
+                     "us_per_launch": round(roof_ms * 1e3, 2),
+                     "us_per_launch_isolated": round(isolated_ms * 1e3, 2)},
         "gpu_launches": wl.launches_per_step() * args.steps,
         "clocks": clock,
     }
     if wl.unit == "GB/s":
         line["pct_of_8tbs"] = round(100 * value / world / NOMINAL_HBM_GBS, 1)
+    if gpu_ref is not None:
+        tv = world * wl.step_units / (gpu_ref["ms_per_step"] * 1e-3) / scale
+        line["triton_value"] = round(tv, 1)
+        line["gpu_reference"] = {"value": round(tv, 1), "unit": wl.unit, "ms_per_step": round(gpu_ref["ms_per_step"], 4),
+                                 "speedup": round(value / tv, 3),
+                                 "what": "the reference's own GPU path, unmodified, on this B200: its Triton kernels "
+                                         "(rope_kv / decode / draft / beam attention), torch SDPA (is_causal) for the "
+                                         "prefill, index_select for the reorder; same inputs, same graph timing"}
+    elif not hasattr(wl, "run_library"):
+        line["triton_value"] = None
+        line["gpu_reference"] = {"unavailable": gpu_ref_why}
     if case_ms is not None:
         line["cases"] = {f"q{t}_L{L}": {"per_gpu_gbs": round(b / (c * 1e-3) / 1e9, 1),
                                         "box_gbs": round(world * b / (c * 1e-3) / 1e9, 1), "us": round(c * 1e3, 1)}

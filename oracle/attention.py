@@ -78,6 +78,16 @@ def prefill_attention(q, k, v, scale=None, dtype=torch.float64):
     return _masked(q.to(dtype), k.to(dtype), v.to(dtype), allowed, scale)
 
 
+def prefill_attention_rows(q, k, v, positions, scale=None, dtype=torch.float64):
+    """The causal prefill at selected query positions only: q/k/v [B, H, W, D], positions [P] -> [B, H, P, D]; query
+    t sees keys [0, t] (the rows of prefill_attention at those positions, for shapes too large to compute whole)."""
+    w = q.size(2)
+    scale = q.size(-1) ** -0.5 if scale is None else scale
+    pos = torch.as_tensor(positions, dtype=torch.long)
+    allowed = torch.arange(w)[None, :] <= pos[:, None]  # [P, W]
+    return _masked(q[:, :, pos].to(dtype), k.to(dtype), v.to(dtype), allowed, scale)
+
+
 def error_stats(got: torch.Tensor, want: torch.Tensor) -> tuple[float, float]:
     """(max-abs, mean-abs) difference in float64."""
     diff = (got.double() - want.double()).abs()

@@ -66,3 +66,14 @@ def beam_inputs(is_bf16: bool, c=BEAM):
     gen_len[-c["beams"]:] = 0  # the last input is finished: no keys at all
     ptr = rng.integers(0, r, (r, c["g"])).astype(np.int32)
     return q, kc, vc, np.array(c["ctx_len"], dtype=np.int64), kg, vg, ptr, gen_len
+
+
+PREFILL = dict(seed=14, b=2, h=1, w=160, d=128)
+PREFILL_D512 = dict(seed=15, b=1, h=1, w=70, d=512)
+
+
+def prefill_inputs(is_bf16: bool, c=PREFILL):
+    """q, k, v [B, H, W, D] of a right-padded prefill (the decoder's views at decode.py:158-171)."""
+    rng = np.random.default_rng(c["seed"])
+    shape = (c["b"], c["h"], c["w"], c["d"])
+    return normal(rng, shape, is_bf16), normal(rng, shape, is_bf16), normal(rng, shape, is_bf16)

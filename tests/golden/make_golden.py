@@ -14,6 +14,12 @@ those files, so they run where the reference is absent. Which reference code pro
                         (modeling.py:396-397), float64; rows of length 0 are zeros (kernels.py:8-9);
 * ``draft_*.npz``    -- the ``tril(past)`` mask + SDPA of ``LLMModel.decoder_forward`` (modeling.py:400-403), float64;
 * ``beam_*.npz``     -- ``BeamDecoder.attention`` on its PyTorch branch (beam.py:215-233), float64 model;
+* ``prefill_*.npz``  -- the prefill's ``F.scaled_dot_product_attention(q, k, v, is_causal=True)`` exactly as
+                        ``GreedyDecoder.prefill_into`` calls it (decode.py:171; reference-order form
+                        modeling.py:398-399), float64 (stored as float32), at head_dim 128 (crossing a 128-position tile) and 512 (the
+                        shipped model's heads);
+* ``accept.npz``     -- not made here: the acceptance rule exists only as the reference's Triton kernel, so
+                        ``make_accept_golden.py`` runs it on a GPU;
 * ``propose.npz``    -- ``reference_propose``, the PyTorch statement of the speculative proposal that the
                         reference's own kernel test checks its Triton kernel against (tests/test_spec.py:43-92,
                         :206-228), on inputs drawn like that test's (few symbols: many partial matches and ties).
@@ -159,6 +165,16 @@ def beam_case(is_bf16: bool):
                         digest=gi.digest(q, kc, vc, ctx_len, kg, vg, ptr, gen_len))
 
 
+def prefill_case(name: str, is_bf16: bool, c: dict):
+    from omniasr_trt import decode
+
+    q, k, v = gi.prefill_inputs(is_bf16, c)
+    qd, kd, vd = (torch.from_numpy(gi.values(a, is_bf16)) for a in (q, k, v))
+    out = decode.F.scaled_dot_product_attention(qd, kd, vd, is_causal=True)  # decode.py:171, torch's SDPA
+    np.savez_compressed(HERE / f"{name}.npz", out=out.numpy().astype(np.float32), digest=gi.digest(q, k, v),
+                        scale=c["d"] ** -0.5)
+
+
 def propose_case(ref_src: str):
     """Twelve trials of 8 rows (proposal lengths 1, 4 and 7), the reference's constants (spec.py:33-39)."""
     from types import SimpleNamespace
@@ -215,6 +231,9 @@ def main():
         decode_case(is_bf16)
         draft_case(is_bf16)
         beam_case(is_bf16)
+    prefill_case("prefill_bf16", True, gi.PREFILL)
+    prefill_case("prefill_f32", False, gi.PREFILL)
+    prefill_case("prefill_bf16_d512", True, gi.PREFILL_D512)
     propose_case(args.reference)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

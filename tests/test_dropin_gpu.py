@@ -262,3 +262,33 @@ def test_public_api_on_these_kernels(ref):
         assert compat.Pipeline(model, {"nbest": 3}).transcribe(inputs, lang=langs) == beam3
     finally:
         llm.SEGMENT = old
+
+
+def sharded_gpu_factory(rank, device):
+    """A launcher worker: the drop-in installed in its own process, the reference's SpecDecoder on ``device``."""
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    from omniasr_b200 import dropin
+
+    dropin.install()
+    from omniasr_trt import modeling, spec
+
+    m = small_model(modeling, seed=21)
+    dec = spec.SpecDecoder(m, draft_tokens=4, max_batch=4, sync_every=3, reserve=8)
+    return lambda shard: dec.generate([c.to(device) for c in shard])
+
+
+def test_sharded_launcher_on_the_gpus(ref):
+    """omniasr_b200.launch.run_sharded over every visible GPU (one worker process each, these kernels dropped in)
+    gives the reference-order greedy tokens, in request order."""
+    from omniasr_b200 import launch
+
+    m = small_model(ref["modeling"], seed=21)
+    t = ref["llm"].LLMTranscriber(m, FakeTokenizer())
+    torch.manual_seed(22)
+    ctxs = [torch.randn(n, 32) for n in (40, 7, 251, 90, 13, 60)]
+    want = [t.greedy_reference(c.cuda()) for c in ctxs]
+    world = min(launch.visible_gpus(), len(ctxs))
+    got = launch.run_sharded(sharded_gpu_factory, ctxs, world, device_type="cuda",
+                             backend="nccl" if world > 1 else None, timeout_s=600)
+    assert got == want

@@ -596,10 +596,28 @@ def test_prefill_attention_other_dtypes(K, dtype, d, w):
 
 
 def test_prefill_attention_config4_shape(K):
-    """BASELINE config 4's prefill: 8 contexts x 1500 positions, 32 x 128 heads (checked on 3 of the heads)."""
+    """BASELINE config 4's prefill: 8 contexts x 1500 positions, 32 x 128 heads. Every (row, head) pair is checked
+    on 40 query positions: the tile edges (0, 127, 128, 1279, 1280, 1499) and 34 drawn per pair."""
     b, h, w, d = 8, 32, 1500, 128
     q, k, v = _prefill_inputs(b, h, w, d, torch.bfloat16, 7)
     out = K.prefill_attention(q, k, v)
-    for hh in (0, 17, 31):
-        want = oatt.prefill_attention(q[:, hh:hh + 1].cpu(), k[:, hh:hh + 1].cpu(), v[:, hh:hh + 1].cpu())
-        check_attention(out[:, hh:hh + 1], want, torch.bfloat16, what=f"config 4 head {hh}")
+    g = torch.Generator().manual_seed(8)
+    qc, kc, vc, oc = q.cpu(), k.cpu(), v.cpu(), out.cpu()
+    edges = torch.tensor([0, 127, 128, 1279, 1280, 1499])
+    for hh in range(h):
+        pos = torch.cat([edges, torch.randint(0, w, (34,), generator=g)]).unique()
+        want = oatt.prefill_attention_rows(qc[:, hh:hh + 1], kc[:, hh:hh + 1], vc[:, hh:hh + 1], pos)
+        check_attention(oc[:, hh:hh + 1, pos], want, torch.bfloat16, what=f"config 4 head {hh}")
+    assert K.read_status() == 0
+
+
+@pytest.mark.parametrize("name,is_bf16,case", [("prefill_bf16", True, gi.PREFILL), ("prefill_f32", False, gi.PREFILL),
+                                               ("prefill_bf16_d512", True, gi.PREFILL_D512)])
+def test_prefill_attention_golden(K, golden, name, is_bf16, case):
+    """Against the reference's own prefill call (SDPA is_causal, decode.py:171) on the golden inputs; bf16 head_dim
+    128 on the tensor cores, fp32 and head_dim 512 on the drafted-verify path."""
+    g = golden(name)
+    q, k, v = (dev(a, is_bf16) for a in gi.prefill_inputs(is_bf16, case))
+    out = K.prefill_attention(q, k, v)
+    check_attention(out, torch.from_numpy(g["out"]), q.dtype, 1e-4, name)
+    assert K.read_status() == 0

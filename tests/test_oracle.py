@@ -145,3 +145,36 @@ def test_accept_oracle_rules():
     assert list(out[3, 98:101]) == [5, 6, 9] and last[3] == 100 and done[3]
     # row 4: finished, untouched
     assert last[4] == 10 and (out[4] == 1).all() and draft_next[4] == 20
+
+
+@pytest.mark.parametrize("name,is_bf16,case", [("prefill_bf16", True, gi.PREFILL), ("prefill_f32", False, gi.PREFILL),
+                                               ("prefill_bf16_d512", True, gi.PREFILL_D512)])
+def test_prefill_oracle(golden, name, is_bf16, case):
+    """The causal prefill (oracle.attention.prefill_attention) against the reference's prefill call, SDPA with
+    is_causal=True as decode.py:171 makes it (float64, stored as float32)."""
+    g = golden(name)
+    q, k, v = gi.prefill_inputs(is_bf16, case)
+    assert gi.digest(q, k, v) == str(g["digest"])
+    out = attention.prefill_attention(_t(q, is_bf16), _t(k, is_bf16), _t(v, is_bf16))
+    np.testing.assert_allclose(out.numpy(), g["out"], atol=2e-6, rtol=1e-6)
+    wrong = attention.prefill_attention(_t(q, is_bf16), _t(k, is_bf16), _t(v, is_bf16).roll(1, dims=2))
+    assert np.abs(wrong.numpy() - g["out"]).max() > 1e-2  # a planted error (values shifted by one key) shows
+
+
+def test_accept_oracle_matches_reference_golden():
+    """The acceptance rule (oracle.spec.accept) against the reference's own Triton kernel (_accept,
+    kernels.py:271-291), whose outputs tests/golden/make_accept_golden.py recorded on a GPU."""
+    from oracle import spec as ospec
+
+    path = GOLDEN / "accept.npz"
+    if not path.exists():
+        pytest.fail("tests/golden/accept.npz is missing: run tests/golden/make_accept_golden.py on a GPU")
+    d = np.load(path)
+    for width in d["widths"]:
+        p = f"w{int(width)}_"
+        state = [d[p + k].copy() for k in ("out", "tok", "last", "done", "draft_next")]
+        ospec.accept(d[p + "tokens"], d[p + "nxt"], *state, d[p + "start"], d[p + "use_draft"], int(d["limit"]),
+                     int(d["eos"]))
+        for got, k in zip(state, ("out", "tok", "last", "done", "draft_next")):
+            assert np.array_equal(got, d[p + k + "_after"]), f"width {int(width)}: {k}"
+        assert not np.array_equal(d[p + "last"], d[p + "last_after"])  # the step advanced some rows

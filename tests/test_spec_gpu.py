@@ -140,3 +140,20 @@ def test_accept_matches_oracle(width):
     for got, want, name in zip(g, w, ("out", "tok", "last", "done", "draft_next")):
         assert np.array_equal(got.cpu().numpy(), want), name
     assert K().read_status(d) == 0
+
+
+def test_accept_matches_reference_golden(golden):
+    """Against the reference's own Triton _accept (kernels.py:271-291), recorded on a GPU by
+    tests/golden/make_accept_golden.py: every state field bit-exact, widths 1, 2, 5 and 9."""
+    d = golden("accept")
+    dev = torch.device(DEVICE)
+    tt = lambda a: torch.as_tensor(a.copy(), device=dev)  # noqa: E731
+    for width in d["widths"]:
+        p = f"w{int(width)}_"
+        g = [tt(d[p + k]) for k in ("out", "tok", "last", "done", "draft_next")]
+        K().accept(tt(d[p + "tokens"]), tt(d[p + "nxt"]), *g, tt(d[p + "start"]), tt(d[p + "use_draft"]),
+                   int(d["limit"]), int(d["eos"]))
+        torch.cuda.synchronize()
+        for got, k in zip(g, ("out", "tok", "last", "done", "draft_next")):
+            assert np.array_equal(got.cpu().numpy(), d[p + k + "_after"]), f"width {int(width)}: {k}"
+    assert K().read_status(dev) == 0
