@@ -103,7 +103,9 @@ class Workload:
     # the event-free step time / layers; "difference" -- the step minus the same step without the dominant calls
     # (both event-free graphs); "events" -- CUDA events around each dominant call in a second graph.
     roof_timing = "whole"
+    dominant_per_layer = 1  # dominant (roofline) calls per layer
     skip_dominant = False  # set while capturing the step without its dominant calls ("difference")
+    gpu_reference_unavailable = None  # why the reference's GPU kernels are not timed on this workload, if so
 
     def __init__(self, device: torch.device, rank: int, world: int, layers: int):
         from omniasr_b200 import kernels
@@ -389,6 +391,7 @@ class Gather(Workload):
         self.roof_units = 2 * rows * self.row_bytes  # read + write of one tensor
         self.step_units = 2 * self.roof_units * self.layers
         self.calls_per_layer = 2
+        self.dominant_per_layer = 2
 
     def layer_in(self, i):
         return [self.parent] if i == 0 else []
@@ -485,6 +488,11 @@ class Sweep(Workload):
 
     name = "sweep"
     roof_timing = "events"  # the roofline call is the largest case (q5, 8192 keys, ~1 ms): events cost nothing there
+    # The reference's Triton split kernel forms its cache offsets in 32-bit arithmetic (kernels.py:172-173,
+    # b * s_kb + h * s_kh): with 64 rows x 32 heads x 8200 positions x 128 dims (2.15e9 elements) they overflow, and on
+    # a B200 it raised an illegal memory access on this workload, so it is not run here.
+    gpu_reference_unavailable = ("the reference's Triton kernels overflow 32-bit cache offsets at 64 rows x 8192 keys "
+                                 "(kernels.py:172-173) and raised an illegal memory access on this workload")
     metric = "decode-attn HBM GB/s, whole box (64 rows sharded, q_len 1/5, lengths 512/2048/8192)"
     roof_kernel = "draft_attention (q_len 5, 8192 keys)"
     traffic_key = "draft_attention_config5_bytes_per_call"
@@ -805,16 +813,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     case_ms = [max_over_ranks(x) for x in per_call] if args.workload == "sweep" else None
     # The roofline call's duration inside the event-free step, so that layers x per call <= ms_per_step.
     if wl.roof_timing == "whole":
-        roof_ms = max_over_ranks(ms / args.steps / wl.layers)
+        roof_ms = max_over_ranks(ms / args.steps / (wl.layers * wl.dominant_per_layer))
     elif wl.roof_timing == "difference":
         wl.skip_dominant = True
         minus_ms = graph_ms(side, device, wl.run, args.steps, args.warmup)
         wl.skip_dominant = False
-        roof_ms = max_over_ranks((ms / args.steps - minus_ms) / wl.layers)
+        roof_ms = max_over_ranks((ms / args.steps - minus_ms) / (wl.layers * wl.dominant_per_layer))
     else:
         roof_ms = isolated_ms
-    roof_how = {"whole": "event-free step time / layers (a step is only the dominant calls)",
-                "difference": "(event-free step - the same step without the dominant calls) / layers",
+    roof_how = {"whole": "event-free step time / dominant calls per step (a step is only the dominant calls)",
+                "difference": "(event-free step - the same step without the dominant calls) / dominant calls per step",
                 "events": "CUDA events around each dominant call, in a second graph replayed after the timed region "
                           "(median of 3)"}[wl.roof_timing]
 
@@ -823,6 +831,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     gpu_ref = None
     if hasattr(wl, "run_library"):
         gpu_ref_why = "this workload's library comparison is cuBLAS (library_baseline)"
+    elif wl.gpu_reference_unavailable:
+        gpu_ref_why = wl.gpu_reference_unavailable
     else:
         ref_ns, gpu_ref_why = reference_gpu_kernels()
         if ref_ns is not None:

@@ -14,7 +14,8 @@
  *
  * `status` (may be NULL) is a device int the kernels OR error bits into: 1 = an index read from a
  * tensor (length, position, slot, beam pointer, parent) was outside its tensor and the access was
- * skipped; 2 = a bounded device wait gave up. The kernels never trap.
+ * skipped; 2 = a bounded device wait gave up; 4 = a kernel found its shared memory not laid out as it
+ * requires and did nothing. The kernels never trap.
  *
  * Each declaration names the function of the reference (Wataru-Nakata/omniasr-trt, Python) it
  * replaces, as path:line within that project.
@@ -129,7 +130,7 @@ int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_str
                               int batch, int heads, int width, int dim, float scale, int dtype, int* status,
                               cudaStream_t stream);
 
-/* Beam reorder: dst row r (r < rows) = src row parent[r], byte-exact; rows are row_bytes long,
+/* Beam reorder: dst row r (r < rows <= 65535) = src row parent[r], byte-exact; rows are row_bytes long,
  * strides in bytes; parent is int32 (parent_is_int64 = 0) or int64. src and dst must not overlap.
  * Replaces the K/V `index_select(0, parent)` of omniasr_trt/llm.py:237-238 and the pointer /
  * history gathers `ptr[parent]`, `hist[parent]` of omniasr_trt/beam.py:175-176. */

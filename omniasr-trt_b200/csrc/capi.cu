@@ -463,6 +463,7 @@ int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_
                            int64_t row_bytes, int* status, cudaStream_t stream) {
   if (int e = check_device()) return e;
   if (rows < 0 || row_bytes < 0 || src_rows < 0) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: sizes");
+  if (rows > 65535) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: %d rows (at most 65535 per call)", rows);
   if (rows == 0 || row_bytes == 0) return ok();
   if (!src || !dst || !parent) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: null pointer");
   if (src_row_stride < row_bytes && src_rows > 1) return fail(OMNIASR_ERR_ARGUMENT, "reorder_gather: src rows overlap");

@@ -19,6 +19,7 @@ namespace omni {
 
 constexpr int kStatusIndex = 1;    // an index read from a tensor was outside its tensor
 constexpr int kStatusTimeout = 2;  // a bounded wait gave up
+constexpr int kStatusLayout = 4;   // a kernel did not run: its shared memory was not laid out as it requires
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 OMNI_DEV void raise_status(int* status, int code) {

@@ -5,20 +5,59 @@
 // one beam's [H, S, D] cache of a layer) and its int32 pointer / token-history reorder
 // `ptr.copy_(ptr[parent])`, `hist.copy_(hist[parent])` (omniasr_trt/beam.py:175-176).
 //
-// An HBM copy: the grid is (row chunks, rows) and every thread moves W-byte words (W = 16 when
-// every address, stride and the row length allow it, else 4 or 1) with four loads in flight
-// before the stores. A parent outside [0, src_rows) skips its row and sets the status word.
+// An HBM copy. When every address, stride and the row length are multiples of 16 bytes (the K/V
+// cache rows always are), block (x, r) copies the x-th 128 KB slab of row r: each thread keeps
+// eight 16-byte loads in flight, with streaming (evict-first) loads and stores, since nothing is
+// read twice. Measured on a B200 over the 40 x 16.8 MB rows of a beam step: 7.15 TB/s, against
+// 6.7 TB/s for torch's index_select and 6.4 TB/s for a grid-stride loop over the flattened rows
+// (a 12-stage TMA bulk-copy ring, one thread per SM, reached 5.6 TB/s). Other alignments use
+// 4- or 1-byte words. A parent outside [0, src_rows) skips its row and sets the status word.
 
 #include "common.cuh"
 #include "gather.cuh"
 
 namespace omni {
 
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 8;                             // 16-byte loads in flight per thread
+constexpr int64_t kSlabWords = kThreads * kUnroll * 4;  // 128 KB of a row per block
+
+OMNI_DEV int64_t parent_of(const GatherArgs& a, int64_t r) {
+  return a.parent64 ? reinterpret_cast<const int64_t*>(a.parent)[r]
+                    : (int64_t) reinterpret_cast<const int32_t*>(a.parent)[r];
+}
+
+__global__ void __launch_bounds__(kThreads) gather_slab_kernel(const GatherArgs a) {
+  const int64_t r = blockIdx.y;
+  const int64_t p = parent_of(a, r);
+  if (p < 0 || p >= a.src_rows) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, kStatusIndex);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.src) + p * a.src_stride);
+  uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dst) + r * a.dst_stride);
+  const int64_t n = a.row_bytes / 16;
+  const int64_t base = (int64_t)blockIdx.x * kSlabWords;
+  const int64_t end = base + kSlabWords < n ? base + kSlabWords : n;
+  for (int64_t i = base + threadIdx.x; i < end; i += kUnroll * kThreads) {
+    uint4 x[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (i + u * kThreads < end) x[u] = __ldcs(s + i + u * kThreads);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (i + u * kThreads < end) __stcs(d + i + u * kThreads, x[u]);
+  }
+}
+
+}  // namespace
+
 template <typename W>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
   const int64_t r = blockIdx.y;
-  const int64_t p = a.parent64 ? reinterpret_cast<const int64_t*>(a.parent)[r]
-                               : (int64_t) reinterpret_cast<const int32_t*>(a.parent)[r];
+  const int64_t p = parent_of(a, r);
   if (p < 0 || p >= a.src_rows) {
     if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, kStatusIndex);
     return;
@@ -42,16 +81,19 @@ cudaError_t launch_gather(const GatherArgs& a, int rows, cudaStream_t stream) {
   if (rows <= 0 || a.row_bytes <= 0) return cudaSuccess;
   const uintptr_t bits = (uintptr_t)a.src | (uintptr_t)a.dst | (uintptr_t)a.src_stride |
                          (uintptr_t)a.dst_stride | (uintptr_t)a.row_bytes;
-  const int w = (bits % 16 == 0) ? 16 : (bits % 4 == 0) ? 4 : 1;
+  if (bits % 16 == 0) {
+    const int64_t slabs = (a.row_bytes / 16 + kSlabWords - 1) / kSlabWords;
+    gather_slab_kernel<<<dim3((unsigned)slabs, (unsigned)rows), kThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
+  const int w = (bits % 4 == 0) ? 4 : 1;
   const int64_t words = a.row_bytes / w;
   const int64_t per_cta = 256 * 4;
   int64_t chunks = (words + per_cta - 1) / per_cta;
   if (chunks > 65535) chunks = 65535;
   if (chunks < 1) chunks = 1;
   dim3 grid((unsigned)chunks, (unsigned)rows);
-  if (w == 16) {
-    gather_rows_kernel<uint4><<<grid, 256, 0, stream>>>(a);
-  } else if (w == 4) {
+  if (w == 4) {
     gather_rows_kernel<uint32_t><<<grid, 256, 0, stream>>>(a);
   } else {
     gather_rows_kernel<uint8_t><<<grid, 256, 0, stream>>>(a);

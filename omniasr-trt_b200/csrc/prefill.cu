@@ -6,15 +6,20 @@
 // sees a later (pad) key.
 //
 // Work unit: (row b, head h, 128-query tile qt) over key tiles 0..qt; units are taken by a persistent grid of one
-// CTA per SM in groups of (b, h) pairs, heaviest first within a group (unit_of). Roles (224 threads):
-//   warp 4  TMA: the query tiles (2 slots; two 64-column boxes, 128-byte swizzle) and the K tiles (3-slot ring)
-//   warp 6  TMA: the V tiles (2-slot ring)
-//   warp 5  MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered), then O += P V with P read
-//           from TMEM (the tcgen05 "A in TMEM" form) and V as an MN-major operand; O accumulates in TMEM
-//   warps 0-3 softmax, thread t = query row t of the tile: the row's 128 scores are loaded into registers at
-//           once, and the max and sum are split over 8 partial accumulators; the running max is raised only when a
-//           row's scores pass it by 2^8, and only then is the row's O rescaled in TMEM
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512) (P: bf16 pairs, 64 columns).
+// CTA per SM in groups of (b, h) pairs, heaviest first within a group (unit_of). Roles (480 threads):
+//   warp 12 TMA: the query tiles (2 slots; two 64-column boxes, 128-byte swizzle) and the K tiles (3-slot ring)
+//   warp 14 TMA: the V tiles (2-slot ring)
+//   warp 13 MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered); then, for each half x of the
+//           tile's keys, O_x += P_x V_x with P_x read from TMEM (the tcgen05 "A in TMEM" form, K = 64 keys)
+//   warps 0-3 / 4-7  softmax warpgroups x = 0 / 1: thread t of warpgroup x owns query row t and the keys
+//           64x .. 64x+63 of every tile. Each keeps its own running max and sum over its half of the keys and its
+//           own accumulator O_x, so the two never synchronise: twice the softmax warps per SM, each with half a
+//           tile's exponentials, on independent chains. The running max is raised only when a row's scores pass it
+//           by 2^8, and only then is the row's O_x rescaled in TMEM. P_x (bf16 pairs) is written over the
+//           warpgroup's own half of S in TMEM.
+//   warps 8-11 epilogue: per unit, O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)),
+//           M = max(m_0, m_1), written as bf16 rows, while the softmax warpgroups start the next unit.
+// TMEM: S0 [0,128) S1 [128,256) O_0 [256,384) O_1 [384,512); P_x of buffer j at columns 128j + 64x .. +32.
 
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -36,10 +41,14 @@ constexpr int QS = 2, KS = 3, VS = 2;
 constexpr int Q_OFF = 0;
 constexpr int K_OFF = Q_OFF + QS * TILE;
 constexpr int V_OFF = K_OFF + KS * TILE;
-constexpr int SMEM_BYTES = V_OFF + VS * TILE + 1024;
-constexpr int THREADS = 224;
+// The tile ring fills the dynamic shared memory exactly: with the 3 KB control block (one static, 1024-aligned
+// struct) the CTA uses 227 KB, the per-block maximum, so there is no room for alignment slack; the kernel checks
+// that the dynamic region starts 1024-aligned (as the 128-byte swizzle needs) and reports status bit 4 otherwise.
+constexpr int SMEM_BYTES = V_OFF + VS * TILE;
+constexpr int THREADS = 480;  // warps 0-7 softmax, 8-11 epilogue, 12 K/Q loads, 13 MMA, 14 V loads
+constexpr int W_EPI = 8, W_LOADK = 12, W_MMA = 13, W_LOADV = 14;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+constexpr uint32_t COL_S = 0, COL_O = 256;  // S buffer j at 128 j; O_x at 256 + 128 x
 constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(BM, D, 0, 1);
 constexpr float kRescale = 8.f;
@@ -92,6 +101,13 @@ OMNI_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 
+// Two floats rounded to bf16 and packed (lo in the low half).
+OMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 OMNI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 OMNI_DEV void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -130,23 +146,43 @@ OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
   h = bh % p.heads;
 }
 
+// The CTA's control block: barriers, the unit's per-row (max, sum) of each half for the epilogue, flags. One static
+// struct, padded to a multiple of 1024 bytes, so that the dynamic tile ring after it starts 1024-aligned.
+struct alignas(1024) Ctl {
+  uint64_t q_full[QS], q_empty[QS], k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
+  uint64_t s_full[2], p_full[2][2], pv_done[2][2], o_ready, o_free, ml_full, ml_free, drain;
+  float2 ml[2][BM];  // [half x][row]
+  uint32_t tmem_base;
+  int abort_flag, issued_k, issued_v, issued_q;  // loads the producers issued
+};
+static_assert(sizeof(Ctl) == 3072, "control block + tile ring = the 227 KB per-block maximum");
+static_assert(sizeof(Ctl) + SMEM_BYTES <= 232448, "shared memory per block");
+
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t q_full[QS], q_empty[QS], k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
-  __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_ready, o_free, drain;
-  __shared__ uint32_t tmem_base;
-  __shared__ volatile int abort_flag;
-  __shared__ volatile int issued_k, issued_v, issued_q;  // loads the producers issued
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ Ctl ctl;
+  uint64_t *q_full = ctl.q_full, *q_empty = ctl.q_empty, *k_full = ctl.k_full, *k_empty = ctl.k_empty;
+  uint64_t *v_full = ctl.v_full, *v_empty = ctl.v_empty, *s_full = ctl.s_full;
+  uint64_t(*p_full)[2] = ctl.p_full;
+  uint64_t(*pv_done)[2] = ctl.pv_done;
+  uint64_t &o_ready = ctl.o_ready, &o_free = ctl.o_free, &ml_full = ctl.ml_full, &ml_free = ctl.ml_free;
+  uint64_t& drain = ctl.drain;
+  float2(*ml_stash)[BM] = ctl.ml;
+  uint32_t& tmem_base = ctl.tmem_base;
+  volatile int& abort_flag = ctl.abort_flag;
+  volatile int &issued_k = ctl.issued_k, &issued_v = ctl.issued_v, &issued_q = ctl.issued_q;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int units = p.batch * p.heads * p.qtiles;
   if ((int)blockIdx.x >= units) return;
+  if (smem_addr(smem) & 1023u) {  // the swizzled tiles need a 1024-aligned ring
+    if (tid == 0) raise_status(p.status, kStatusLayout);
+    return;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < QS; ++s) {
@@ -161,33 +197,40 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&pv_done[s], 1);
-      mbar_init(&s_free[s], 128);
-      mbar_init(&p_full[s], 128);
-    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    for (int x = 0; x < 2; ++x)
+      for (int j = 0; j < 2; ++j) {
+        mbar_init(&p_full[x][j], 128);
+        mbar_init(&pv_done[x][j], 1);
+      }
     mbar_init(&o_ready, 1);
     mbar_init(&o_free, 128);
+    mbar_init(&ml_full, 256);
+    mbar_init(&ml_free, 128);
     mbar_init(&drain, 1);
     mbar_fence_init();
     abort_flag = 0;
     issued_k = issued_v = issued_q = 0;
   }
-  if (tid == 0) OMNI_TRACE_AT(4000);
-  if (warp == 0) tmem_alloc(&tmem_base, TMEM_COLS);
+  if (warp == W_EPI) tmem_alloc(&tmem_base, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (tid == 0) OMNI_TRACE_AT(4001);
   grid_dependency_wait();  // q, k, v may come from the kernel before (launched as a programmatic dependent)
   const uint32_t tbase = tmem_base;
   unsigned char* qs = smem + Q_OFF;
+  // Every wait gives up at once when another role has given up (abort_flag), else after the bounded time.
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (mbar_wait_or(bar, parity, &abort_flag)) return true;
+    abort_flag = 1;
+    return false;
+  };
 
-  if (warp == 4 || warp == 6) {
+  if (warp == W_LOADK || warp == W_LOADV) {
     // ------------------------------------------------------------------ producers
     if (lane == 0) {
-      const bool is_k = warp == 4;
+      const bool is_k = warp == W_LOADK;
       prefetch_tmap(is_k ? &kmap : &vmap);
       if (is_k) prefetch_tmap(&qmap);
       int tile = 0, nunit = 0;
@@ -196,10 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         unit_of(p, u, b, h, qt);
         if (is_k) {
           const int qslot = nunit % QS, quse = nunit / QS;
-          if (quse >= 1 && !mbar_wait(&q_empty[qslot], (quse - 1) & 1)) {
-            abort_flag = 1;
-            break;
-          }
+          if (quse >= 1 && !wait(&q_empty[qslot], (quse - 1) & 1)) break;
           mbar_arrive_expect_tx(&q_full[qslot], TILE);
           tma_load_4d(qs + qslot * TILE, &qmap, 0, qt * BM, h, b, &q_full[qslot]);
           tma_load_4d(qs + qslot * TILE + BOX, &qmap, 64, qt * BM, h, b, &q_full[qslot]);
@@ -210,61 +250,55 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int slot = tile % ns, use = tile / ns;
           uint64_t* empty = is_k ? &k_empty[slot] : &v_empty[slot];
           uint64_t* full = is_k ? &k_full[slot] : &v_full[slot];
-          if (use >= 1 && !mbar_wait(empty, (use - 1) & 1)) {
-            abort_flag = 1;
-            break;
-          }
+          if (use >= 1 && !wait(empty, (use - 1) & 1)) break;
           unsigned char* dst = smem + (is_k ? K_OFF : V_OFF) + slot * TILE;
           mbar_arrive_expect_tx(full, TILE);
           tma_load_4d(dst, is_k ? &kmap : &vmap, 0, kt * BN, h, b, full);
           tma_load_4d(dst + BOX, is_k ? &kmap : &vmap, 64, kt * BN, h, b, full);
           if (is_k) issued_k = tile + 1;
           else issued_v = tile + 1;
-          OMNI_TRACE_AT(tile * 8 + (is_k ? 0 : 1));
         }
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int tile = 0, nunit = 0, qslot = 0;
       bool ok = true;
-      auto scores = [&](int t, int kt_local) -> bool {  // S[t & 1] = Q K(t)^T
-        const int sb = t & 1, su = t >> 1;
+      auto scores = [&](int t) -> bool {  // S[t & 1] = Q K(t)^T (S[t & 1] was last read by O += P(t - 2) V)
         const int slot = t % KS;
-        if (su >= 1 && !mbar_wait(&s_free[sb], (su - 1) & 1)) return false;
-        if (!mbar_wait(&k_full[slot], (t / KS) & 1)) return false;
+        if (!wait(&k_full[slot], (t / KS) & 1)) return false;
         tc_fence_after();
-        OMNI_TRACE_AT(t * 8 + 2);
         const uint32_t qa = smem_addr(qs + qslot * TILE), ka = smem_addr(smem + K_OFF + slot * TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t a = smem_desc(qa + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
           const uint64_t bd = smem_desc(ka + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-          mma_bf16_ss(tbase + COL_S + sb * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tbase + COL_S + (t & 1) * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[sb]);
+        tc_commit(&s_full[t & 1]);
         tc_commit(&k_empty[slot]);
-        (void)kt_local;
         return true;
       };
-      auto values = [&](int t, bool first_of_unit) -> bool {  // O += P[t & 1] V(t)
+      auto values = [&](int t, bool first_of_unit) -> bool {  // O_x += P_x(t) V_x(t), x = 0, 1
         const int pb = t & 1, pu = t >> 1;
         const int slot = t % VS;
-        if (first_of_unit && nunit >= 1 && !mbar_wait(&o_free, (nunit - 1) & 1)) return false;
-        if (!mbar_wait(&p_full[pb], pu & 1)) return false;
-        if (!mbar_wait(&v_full[slot], (t / VS) & 1)) return false;
-        tc_fence_after();
-        OMNI_TRACE_AT(t * 8 + 3);
+        if (first_of_unit && nunit >= 1 && !wait(&o_free, (nunit - 1) & 1)) return false;
+        if (!wait(&v_full[slot], (t / VS) & 1)) return false;
         const uint32_t va = smem_addr(smem + V_OFF + slot * TILE);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = smem_desc(va + kk * 2048, BOX, 1024, kLayoutSw128);
-          mma_bf16_ts(tbase + COL_O, tbase + COL_P + pb * 64 + kk * 8, bd, IDESC_O,
-                      (first_of_unit && kk == 0) ? 0u : 1u);
+        for (int x = 0; x < 2; ++x) {
+          if (!wait(&p_full[x][pb], pu & 1)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bd = smem_desc(va + (4 * x + kk) * 2048, BOX, 1024, kLayoutSw128);
+            mma_bf16_ts(tbase + COL_O + x * 128, tbase + COL_S + pb * 128 + x * 64 + kk * 8, bd, IDESC_O,
+                        (first_of_unit && kk == 0) ? 0u : 1u);
+          }
+          tc_commit(&pv_done[x][pb]);
         }
-        tc_commit(&pv_done[pb]);
         tc_commit(&v_empty[slot]);
         return true;
       };
@@ -272,13 +306,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         int b, h, qt;
         unit_of(p, u, b, h, qt);
         qslot = nunit % QS;
-        if (!mbar_wait(&q_full[qslot], (nunit / QS) & 1)) {
+        if (!wait(&q_full[qslot], (nunit / QS) & 1)) {
           ok = false;
           break;
         }
         const int t0 = tile;
         for (int kt = 0; kt <= qt && ok; ++kt, ++tile) {
-          ok = scores(tile, kt);
+          ok = scores(tile);
           if (ok && kt == qt) tc_commit(&q_empty[qslot]);  // the unit's last use of Q
           if (ok && kt > 0) ok = values(tile - 1, tile - 1 == t0);
         }
@@ -288,144 +322,155 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) abort_flag = 1;
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------------ softmax (thread = query row)
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+  } else if (warp < 8) {
+    // ------------------------------------------------------------------ softmax, half x of every tile's keys
+    const int x = warp >> 2;
+    const int row = tid & 127;  // query row within the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t col_o = tbase + lane_off + COL_O + x * 128;
     int tile = 0, nunit = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++nunit) {
+    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
       float m = -INFINITY, l = 0.f;
       for (int kt = 0; kt <= qt; ++kt, ++tile) {
         const int sb = tile & 1;
-        const uint32_t spar = (tile >> 1) & 1;
-        const bool diag = kt == qt;
-        if (tid == 0) OMNI_TRACE_AT(tile * 8 + 7);
-        if (!mbar_wait(&s_full[sb], spar)) abort_flag = 1;
-        if (tid == 0) OMNI_TRACE_AT(tile * 8 + 4);
+        if (!wait(&s_full[sb], (tile >> 1) & 1)) break;
         tc_fence_after();
         __syncwarp();
-        const uint32_t scol = tbase + lane_off + COL_S + sb * 128;
-        // The row's 128 scores in registers: four loads in flight, one wait.
-        uint32_t raw[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32_async(scol + c * 32, raw + c * 32);
+        const uint32_t scol = tbase + lane_off + COL_S + sb * 128 + x * 64;
+        uint32_t raw[64];
+        tmem_ld32_async(scol, raw);
+        tmem_ld32_async(scol + 32, raw + 32);
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&s_free[sb]);  // S[sb] is in registers: the next-but-one Q K^T may overwrite it
-        float v[128];
+        float v[64];
 #pragma unroll
-        for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(raw[i]);
-        if (diag) {  // keys past the query
+        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(raw[i]);
+        if (kt == qt) {  // the diagonal tile: keys past the query
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i > tid) v[i] = -INFINITY;
+          for (int i = 0; i < 64; ++i)
+            if (x * 64 + i > row) v[i] = -INFINITY;
         }
         float part[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) part[j] = v[j];
 #pragma unroll
-        for (int i = 8; i < 128; ++i) part[i & 7] = fmaxf(part[i & 7], v[i]);
-        float tmax = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
-                           fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7])));
-        tmax *= p.qscale;
-        if (tid == 0) OMNI_TRACE_AT(tile * 8 + 5);
-        // Raise the running max only when needed; then the row's O (built from earlier tiles) is rescaled.
-        float mnew = m;
-        if (tmax > m + kRescale) mnew = tmax;
+        for (int i = 8; i < 64; ++i) part[i & 7] = fmaxf(part[i & 7], v[i]);
+        const float tmax = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
+                                 fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7]))) * p.qscale;
+        // Raise the running max only when needed; then this half's O (built from earlier tiles) is rescaled. The
+        // probabilities are formed first, so that the scores are dead while O is rescaled (register pressure).
+        const float mnew = tmax > m + kRescale ? tmax : m;
         const bool rescale = mnew != m && kt > 0;
+        const float mm = mnew == -INFINITY ? 0.f : mnew;  // a row with no key in this half yet: every p is 0
+        uint32_t w[32];
+        float ls[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ls[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2(fmaf(v[2 * i], p.qscale, -mm));
+          const float p1 = ex2(fmaf(v[2 * i + 1], p.qscale, -mm));
+          ls[(2 * i) & 7] += p0;
+          ls[(2 * i + 1) & 7] += p1;
+          w[i] = pack_bf16x2(p0, p1);
+        }
         if (__any_sync(0xffffffffu, rescale)) {
-          if (!mbar_wait(&pv_done[(tile - 1) & 1], ((tile - 1) >> 1) & 1)) abort_flag = 1;
+          if (!wait(&pv_done[x][(tile - 1) & 1], ((tile - 1) >> 1) & 1)) break;
           tc_fence_after();
           __syncwarp();
           const float sc = rescale ? ex2(m - mnew) : 1.f;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float o[32];
-            uint32_t w[32];
-            tmem_ld32(tbase + lane_off + COL_O + c * 32, o);
+            uint32_t ow[32];
+            tmem_ld32(col_o + c * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * sc);
-            tmem_st32(tbase + lane_off + COL_O + c * 32, w);
+            for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(o[i] * sc);
+            tmem_st32(col_o + c * 32, ow);
           }
           tmem_wait_st();
           l *= sc;
         }
         m = mnew;
-        // P[sb] is free once O += P V of two tiles ago has completed.
-        if (tile >= 2) {
-          if (!mbar_wait(&pv_done[sb], ((tile - 2) >> 1) & 1)) abort_flag = 1;
-          tc_fence_after();
-          __syncwarp();
-        }
-        // Probabilities (bf16 pairs) into P[sb], and the row sum.
-        uint32_t w[64];
-        float ls[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ls[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float p0 = ex2(fmaf(v[2 * i], p.qscale, -m));
-          const float p1 = ex2(fmaf(v[2 * i + 1], p.qscale, -m));
-          ls[(2 * i) & 7] += p0;
-          ls[(2 * i + 1) & 7] += p1;
-          const __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
-          w[i] = *reinterpret_cast<const uint32_t*>(&pk);
-        }
         l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-#pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_st32(tbase + lane_off + COL_P + sb * 64 + c * 32, w + c * 32);
+        tmem_st32(scol, w);  // over this half's scores, which are in registers already
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[sb]);
-        if (tid == 0) OMNI_TRACE_AT(tile * 8 + 6);
+        mbar_arrive(&p_full[x][sb]);
       }
-      // Epilogue: O / l -> out[b, q, h, :] for the tile's valid queries.
-      if (!mbar_wait(&o_ready, nunit & 1)) abort_flag = 1;
+      if (abort_flag) break;
+      // The unit's (max, sum) of this half for the epilogue, once the epilogue has read the previous unit's: a unit
+      // of one or two tiles can be finished before that, and ml_full must not complete two phases ahead of its
+      // waiter.
+      if (nunit >= 1 && !wait(&ml_free, (nunit - 1) & 1)) break;
+      ml_stash[x][row] = make_float2(m, l);
+      mbar_arrive(&ml_full);
+    }
+  } else if (warp < 12) {
+    // ------------------------------------------------------------------ epilogue (thread = query row)
+    const int row = tid & 127;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    int nunit = 0;
+    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
+      int b, h, qt;
+      unit_of(p, u, b, h, qt);
+      if (!wait(&o_ready, nunit & 1)) break;
+      if (!wait(&ml_full, nunit & 1)) break;
       tc_fence_after();
       __syncwarp();
-      const int q = qt * BM + tid;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float2 e0 = ml_stash[0][row], e1 = ml_stash[1][row];
+      mbar_arrive(&ml_free);
+      const float mx = fmaxf(e0.x, e1.x);
+      const float a0 = e0.y > 0.f ? ex2(e0.x - mx) : 0.f;
+      const float a1 = e1.y > 0.f ? ex2(e1.x - mx) : 0.f;
+      const float den = e0.y * a0 + e1.y * a1;
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      const float f0 = a0 * inv, f1 = a1 * inv;
+      const int q = qt * BM + row;
       __nv_bfloat16* dst = p.out + (int64_t)b * p.out_sb + (int64_t)q * p.out_sw + (int64_t)h * p.out_sh;
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(tbase + lane_off + COL_O + c * 32, v);
+        uint32_t r0[32], r1[32];
+        tmem_ld32_async(tbase + lane_off + COL_O + c * 32, r0);
+        tmem_ld32_async(tbase + lane_off + COL_O + 128 + c * 32, r1);
+        tmem_wait_ld();
         if (q < p.width) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            uint32_t w[4];
+            uint32_t w4[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              w[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[8 * i + 2 * j] * inv)) |
-                     ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[8 * i + 2 * j + 1] * inv)) << 16);
-            *reinterpret_cast<uint4*>(dst + c * 32 + i * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int j = 0; j < 4; ++j) {
+              const int k = 8 * i + 2 * j;
+              const float lo = fmaf(__uint_as_float(r0[k]), f0, __uint_as_float(r1[k]) * f1);
+              const float hi = fmaf(__uint_as_float(r0[k + 1]), f0, __uint_as_float(r1[k + 1]) * f1);
+              w4[j] = pack_bf16x2(lo, hi);
+            }
+            *reinterpret_cast<uint4*>(dst + c * 32 + i * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&o_free);
-      if (abort_flag) break;
     }
   }
   __syncthreads();
   if (abort_flag) {
     if (tid == 0) raise_status(p.status, kStatusTimeout);
-    if (tid == 5 * 32) {
-      tc_commit(&drain);
+    if (tid == W_MMA * 32) {
+      tc_commit(&drain);  // every MMA the issuer thread issued has completed once this arrives
       mbar_wait(&drain, 0);
     }
-  }
-  __syncthreads();
-  if (abort_flag && tid == 4 * 32) {
-    // Let the latest load of every slot land (a slot is refilled only after its previous load was consumed).
-    for (int i = issued_k > KS ? issued_k - KS : 0; i < issued_k; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1);
-    for (int i = issued_v > VS ? issued_v - VS : 0; i < issued_v; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1);
-    for (int i = issued_q > QS ? issued_q - QS : 0; i < issued_q; ++i) mbar_wait(&q_full[i % QS], (i / QS) & 1);
+    if (tid == W_LOADK * 32) {
+      // Let the latest load of every slot land (a slot is refilled only after its previous load was consumed).
+      for (int i = issued_k > KS ? issued_k - KS : 0; i < issued_k; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1);
+      for (int i = issued_v > VS ? issued_v - VS : 0; i < issued_v; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1);
+      for (int i = issued_q > QS ? issued_q - QS : 0; i < issued_q; ++i) mbar_wait(&q_full[i % QS], (i / QS) & 1);
+    }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == W_EPI) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }
