@@ -6,20 +6,21 @@
 // sees a later (pad) key.
 //
 // Work unit: (row b, head h, 128-query tile qt) over key tiles 0..qt; units are taken by a persistent grid of one
-// CTA per SM in groups of (b, h) pairs, heaviest first within a group (unit_of). Roles (480 threads):
-//   warp 12 TMA: the query tiles (2 slots; two 64-column boxes, 128-byte swizzle) and the K tiles (3-slot ring)
-//   warp 14 TMA: the V tiles (2-slot ring)
-//   warp 13 MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered); then, for each half x of the
-//           tile's keys, O_x += P_x V_x with P_x read from TMEM (the tcgen05 "A in TMEM" form, K = 64 keys)
-//   warps 0-3 / 4-7  softmax warpgroups x = 0 / 1: thread t of warpgroup x owns query row t and the keys
-//           64x .. 64x+63 of every tile. Each keeps its own running max and sum over its half of the keys and its
-//           own accumulator O_x, so the two never synchronise: twice the softmax warps per SM, each with half a
-//           tile's exponentials, on independent chains. The running max is raised only when a row's scores pass it
-//           by 2^8, and only then is the row's O_x rescaled in TMEM. P_x (bf16 pairs) is written over the
-//           warpgroup's own half of S in TMEM.
-//   warps 8-11 epilogue: per unit, O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)),
-//           M = max(m_0, m_1), written as bf16 rows, while the softmax warpgroups start the next unit.
-// TMEM: S0 [0,128) S1 [128,256) O_0 [256,384) O_1 [384,512); P_x of buffer j at columns 128j + 64x .. +32.
+// CTA per SM in groups of (b, h) pairs, heaviest first within a group (unit_of). Roles (512 threads):
+//   warp 12 TMA: the K tiles (3-slot ring, two 64-column boxes each, 128-byte swizzle); warp 14 TMA: the V tiles
+//   warp 13 MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered) with Q read from TMEM (the
+//           tcgen05 "A in TMEM" form); warp 15 MMA: O += P V with P read from TMEM as well. Two issuing threads,
+//           because one thread issues a tcgen05.mma in about 55 clocks at best (measured), while a 128x128x16 MMA
+//           takes the tensor core about 64: a single issuer with its waits left the tensor core idle half the time.
+//           Only K and V come from shared memory.
+//   warps 0-3 / 4-7  softmax warpgroups x = 0 / 1: thread t of warpgroup x owns query row t and the keys 64x .. 64x+63
+//           of every tile, so twice the softmax warps per SM each form half a tile's exponentials. The two keep one
+//           running max per row: each tile one barrier over both warpgroups asks whether any row's scores pass its
+//           max by 2^8 (log2 units); only then are the tile maxima exchanged, the max raised and O rescaled in TMEM
+//           (each warpgroup its 64 head dims). P (bf16 pairs) is written over the warpgroup's half of S in TMEM.
+//   warps 8-11 Q loader and epilogue: per unit, the next unit's query rows into TMEM (thread t = row t), then
+//           O / (l_0 + l_1) of this unit as bf16 rows, while the softmax warpgroups go on with the next unit.
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) Q0 [384,448) Q1 [448,512); P of S buffer j, half x at 128j + 64x .. +32.
 
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -37,18 +38,18 @@ constexpr int BM = 128;  // queries per tile
 constexpr int BN = 128;  // keys per tile
 constexpr int TILE = BN * D * 2;
 constexpr int BOX = BN * 64 * 2;
-constexpr int QS = 2, KS = 3, VS = 2;
-constexpr int Q_OFF = 0;
-constexpr int K_OFF = Q_OFF + QS * TILE;
+constexpr int KS = 3, VS = 3;
+constexpr int K_OFF = 0;
 constexpr int V_OFF = K_OFF + KS * TILE;
-// The tile ring fills the dynamic shared memory exactly: with the 3 KB control block (one static, 1024-aligned
-// struct) the CTA uses 227 KB, the per-block maximum, so there is no room for alignment slack; the kernel checks
-// that the dynamic region starts 1024-aligned (as the 128-byte swizzle needs) and reports status bit 4 otherwise.
 constexpr int SMEM_BYTES = V_OFF + VS * TILE;
-constexpr int THREADS = 480;  // warps 0-7 softmax, 8-11 epilogue, 12 K/Q loads, 13 MMA, 14 V loads
-constexpr int W_EPI = 8, W_LOADK = 12, W_MMA = 13, W_LOADV = 14;
+constexpr int NWG = 2;        // softmax warpgroups; warpgroup x owns keys KW x .. KW x + KW - 1 of every tile
+constexpr int KW = BN / NWG;  // keys per softmax warpgroup (a multiple of the 16-key MMA step)
+constexpr int DW = D / NWG;   // head dims of O each softmax warpgroup rescales
+constexpr int W_EPI = 4 * NWG, W_LOADK = W_EPI + 4, W_MMA = W_LOADK + 1, W_LOADV = W_LOADK + 2, W_MMA_PV = W_LOADK + 3;
+constexpr int THREADS = 32 * (W_MMA_PV + 1);  // softmax, Q loader + epilogue, K loads, S MMAs, V loads, PV MMAs
+constexpr int SM_THREADS = 128 * NWG;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_O = 256;  // S buffer j at 128 j; O_x at 256 + 128 x
+constexpr uint32_t COL_S = 0, COL_O = 256, COL_Q = 384;  // S buffer j at 128 j; Q buffer j at 384 + 64 j
 constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(BM, D, 0, 1);
 constexpr float kRescale = 8.f;
@@ -57,6 +58,8 @@ struct Params {
   int batch, heads, width, qtiles;
   int group;  // (row, head) pairs per scheduling group
   float qscale;  // scale * log2(e)
+  const __nv_bfloat16* q;
+  int64_t q_sb, q_sh, q_sw;  // q[b, h, w, :] strides (elements)
   __nv_bfloat16* out;
   int64_t out_sb, out_sw, out_sh;  // out[b, w, h, :] strides (elements)
   int* status;
@@ -146,33 +149,44 @@ OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
   h = bh % p.heads;
 }
 
-// The CTA's control block: barriers, the unit's per-row (max, sum) of each half for the epilogue, flags. One static
-// struct, padded to a multiple of 1024 bytes, so that the dynamic tile ring after it starts 1024-aligned.
+// The CTA's control block: barriers, the row maxima exchanged between the softmax warpgroups, the unit's row sums
+// for the epilogue, flags. One static struct, padded to 1024 bytes, so that the dynamic tile ring after it starts
+// 1024-aligned (the kernel checks, and reports status bit 4 otherwise).
 struct alignas(1024) Ctl {
-  uint64_t q_full[QS], q_empty[QS], k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
-  uint64_t s_full[2], p_full[2][2], pv_done[2][2], o_ready, o_free, ml_full, ml_free, drain;
-  float2 ml[2][BM];  // [half x][row]
+  uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], q_full[2], q_free[2];
+  uint64_t s_full[2], p_full[NWG][2], pv_done[2], o_ready, o_free, l_full, l_free, drain;
+  float tmax[NWG][BM];  // [warpgroup][row]: a tile's scaled row maxima, on the rare tiles that raise a max
+  float lsum[NWG][BM];  // [warpgroup][row]: the unit's row sums for the epilogue
   uint32_t tmem_base;
-  int abort_flag, issued_k, issued_v, issued_q;  // loads the producers issued
+  int abort_flag, issued_k, issued_v;  // loads the producers issued
 };
-static_assert(sizeof(Ctl) == 3072, "control block + tile ring = the 227 KB per-block maximum");
 static_assert(sizeof(Ctl) + SMEM_BYTES <= 232448, "shared memory per block");
 
+OMNI_DEV bool sync_or(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+    prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   const Params p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ Ctl ctl;
-  uint64_t *q_full = ctl.q_full, *q_empty = ctl.q_empty, *k_full = ctl.k_full, *k_empty = ctl.k_empty;
-  uint64_t *v_full = ctl.v_full, *v_empty = ctl.v_empty, *s_full = ctl.s_full;
+  uint64_t *k_full = ctl.k_full, *k_empty = ctl.k_empty, *v_full = ctl.v_full, *v_empty = ctl.v_empty;
+  uint64_t *q_full = ctl.q_full, *q_free = ctl.q_free, *s_full = ctl.s_full, *pv_done = ctl.pv_done;
   uint64_t(*p_full)[2] = ctl.p_full;
-  uint64_t(*pv_done)[2] = ctl.pv_done;
-  uint64_t &o_ready = ctl.o_ready, &o_free = ctl.o_free, &ml_full = ctl.ml_full, &ml_free = ctl.ml_free;
+  uint64_t &o_ready = ctl.o_ready, &o_free = ctl.o_free, &l_full = ctl.l_full, &l_free = ctl.l_free;
   uint64_t& drain = ctl.drain;
-  float2(*ml_stash)[BM] = ctl.ml;
-  uint32_t& tmem_base = ctl.tmem_base;
   volatile int& abort_flag = ctl.abort_flag;
-  volatile int &issued_k = ctl.issued_k, &issued_v = ctl.issued_v, &issued_q = ctl.issued_q;
+  volatile int &issued_k = ctl.issued_k, &issued_v = ctl.issued_v;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -185,10 +199,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   if (tid == 0) {
-    for (int s = 0; s < QS; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-    }
     for (int s = 0; s < KS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -197,29 +207,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    for (int x = 0; x < 2; ++x)
-      for (int j = 0; j < 2; ++j) {
-        mbar_init(&p_full[x][j], 128);
-        mbar_init(&pv_done[x][j], 1);
-      }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&q_full[j], 128);
+      mbar_init(&q_free[j], 1);
+      mbar_init(&s_full[j], 1);
+      mbar_init(&pv_done[j], 1);
+      for (int x = 0; x < NWG; ++x) mbar_init(&p_full[x][j], 128);
+    }
     mbar_init(&o_ready, 1);
     mbar_init(&o_free, 128);
-    mbar_init(&ml_full, 256);
-    mbar_init(&ml_free, 128);
-    mbar_init(&drain, 1);
+    mbar_init(&l_full, SM_THREADS);
+    mbar_init(&l_free, 128);
+    mbar_init(&drain, 2);
     mbar_fence_init();
     abort_flag = 0;
-    issued_k = issued_v = issued_q = 0;
+    issued_k = issued_v = 0;
   }
-  if (warp == W_EPI) tmem_alloc(&tmem_base, TMEM_COLS);
+  if (warp == W_EPI) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   grid_dependency_wait();  // q, k, v may come from the kernel before (launched as a programmatic dependent)
-  const uint32_t tbase = tmem_base;
-  unsigned char* qs = smem + Q_OFF;
+  if (tid == 0) OMNI_TRACE_AT(1599);
+  OMNI_TRACE_CTA(0);
+  const uint32_t tbase = ctl.tmem_base;
   // Every wait gives up at once when another role has given up (abort_flag), else after the bounded time.
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
     if (mbar_wait_or(bar, parity, &abort_flag)) return true;
@@ -231,209 +242,284 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------ producers
     if (lane == 0) {
       const bool is_k = warp == W_LOADK;
-      prefetch_tmap(is_k ? &kmap : &vmap);
-      if (is_k) prefetch_tmap(&qmap);
-      int tile = 0, nunit = 0;
-      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
+      prefetch_tmap(map);
+      const int ns = is_k ? KS : VS;
+      unsigned char* ring = smem + (is_k ? K_OFF : V_OFF);
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      int tile = 0;
+      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
-        if (is_k) {
-          const int qslot = nunit % QS, quse = nunit / QS;
-          if (quse >= 1 && !wait(&q_empty[qslot], (quse - 1) & 1)) break;
-          mbar_arrive_expect_tx(&q_full[qslot], TILE);
-          tma_load_4d(qs + qslot * TILE, &qmap, 0, qt * BM, h, b, &q_full[qslot]);
-          tma_load_4d(qs + qslot * TILE + BOX, &qmap, 64, qt * BM, h, b, &q_full[qslot]);
-          issued_q = nunit + 1;
-        }
         for (int kt = 0; kt <= qt && !abort_flag; ++kt, ++tile) {
-          const int ns = is_k ? KS : VS;
           const int slot = tile % ns, use = tile / ns;
-          uint64_t* empty = is_k ? &k_empty[slot] : &v_empty[slot];
-          uint64_t* full = is_k ? &k_full[slot] : &v_full[slot];
-          if (use >= 1 && !wait(empty, (use - 1) & 1)) break;
-          unsigned char* dst = smem + (is_k ? K_OFF : V_OFF) + slot * TILE;
-          mbar_arrive_expect_tx(full, TILE);
-          tma_load_4d(dst, is_k ? &kmap : &vmap, 0, kt * BN, h, b, full);
-          tma_load_4d(dst + BOX, is_k ? &kmap : &vmap, 64, kt * BN, h, b, full);
+          if (use >= 1 && !wait(&empty[slot], (use - 1) & 1)) break;
+          mbar_arrive_expect_tx(&full[slot], TILE);
+          tma_load_4d(ring + slot * TILE, map, 0, kt * BN, h, b, &full[slot]);
+          tma_load_4d(ring + slot * TILE + BOX, map, 64, kt * BN, h, b, &full[slot]);
           if (is_k) issued_k = tile + 1;
           else issued_v = tile + 1;
+          OMNI_TRACE_AT(tile * 8 + (is_k ? 0 : 1));
         }
       }
     }
     __syncwarp();
   } else if (warp == W_MMA) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ S issuer: S[t & 1] = Q K(t)^T
+    // S[t & 1] is free once O += P(t - 2) V has completed (P(t - 2) lies over it); its own Q buffer stays until the
+    // unit's last S has completed (q_free).
     if (lane == 0) {
-      int tile = 0, nunit = 0, qslot = 0;
+      // Slot s's descriptor is slot 0's with the start address (in 16-byte units, 14 bits) moved on by s tiles.
+      const uint64_t kdesc0 = smem_desc(smem_addr(smem + K_OFF), 16, 1024, kLayoutSw128);
+      int tile = 0, nunit = 0;
       bool ok = true;
-      auto scores = [&](int t) -> bool {  // S[t & 1] = Q K(t)^T (S[t & 1] was last read by O += P(t - 2) V)
-        const int slot = t % KS;
-        if (!wait(&k_full[slot], (t / KS) & 1)) return false;
-        tc_fence_after();
-        const uint32_t qa = smem_addr(qs + qslot * TILE), ka = smem_addr(smem + K_OFF + slot * TILE);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = smem_desc(qa + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-          const uint64_t bd = smem_desc(ka + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-          mma_bf16_ss(tbase + COL_S + (t & 1) * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[t & 1]);
-        tc_commit(&k_empty[slot]);
-        return true;
-      };
-      auto values = [&](int t, bool first_of_unit) -> bool {  // O_x += P_x(t) V_x(t), x = 0, 1
-        const int pb = t & 1, pu = t >> 1;
-        const int slot = t % VS;
-        if (first_of_unit && nunit >= 1 && !wait(&o_free, (nunit - 1) & 1)) return false;
-        if (!wait(&v_full[slot], (t / VS) & 1)) return false;
-        const uint32_t va = smem_addr(smem + V_OFF + slot * TILE);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          if (!wait(&p_full[x][pb], pu & 1)) return false;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = smem_desc(va + (4 * x + kk) * 2048, BOX, 1024, kLayoutSw128);
-            mma_bf16_ts(tbase + COL_O + x * 128, tbase + COL_S + pb * 128 + x * 64 + kk * 8, bd, IDESC_O,
-                        (first_of_unit && kk == 0) ? 0u : 1u);
-          }
-          tc_commit(&pv_done[x][pb]);
-        }
-        tc_commit(&v_empty[slot]);
-        return true;
-      };
       for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
-        qslot = nunit % QS;
-        if (!wait(&q_full[qslot], (nunit / QS) & 1)) {
-          ok = false;
-          break;
+        const int qb = nunit & 1;
+        if (!wait(&q_full[qb], (nunit >> 1) & 1)) break;
+        const uint32_t qcol = tbase + COL_Q + qb * 64;
+        for (int kt = 0; kt <= qt; ++kt, ++tile) {
+          const int slot = tile % KS;
+          if (tile >= 2 && !wait(&pv_done[tile & 1], ((tile - 2) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          if (!wait(&k_full[slot], (tile / KS) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dcol = tbase + COL_S + (tile & 1) * 128;
+          const uint64_t kd = kdesc0 + (uint64_t)(slot * (TILE >> 4));
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_bf16_ts(dcol, qcol + kk * 8, kd + (uint64_t)((((kk >> 2) * BOX + (kk & 3) * 32) >> 4)), IDESC_S,
+                        kk > 0 ? 1u : 0u);
+          tc_commit(&s_full[tile & 1]);
+          tc_commit(&k_empty[slot]);
+          if (kt == qt) tc_commit(&q_free[qb]);  // the unit's last read of its Q buffer
+          OMNI_TRACE_AT(tile * 8 + 2);
         }
-        const int t0 = tile;
-        for (int kt = 0; kt <= qt && ok; ++kt, ++tile) {
-          ok = scores(tile);
-          if (ok && kt == qt) tc_commit(&q_empty[qslot]);  // the unit's last use of Q
-          if (ok && kt > 0) ok = values(tile - 1, tile - 1 == t0);
-        }
-        if (ok) ok = values(tile - 1, tile - 1 == t0);
-        if (ok) tc_commit(&o_ready);
       }
-      if (!ok) abort_flag = 1;
     }
     __syncwarp();
-  } else if (warp < 8) {
-    // ------------------------------------------------------------------ softmax, half x of every tile's keys
+  } else if (warp == W_MMA_PV) {
+    // ------------------------------------------------------------------ PV issuer: O += P(t) V(t)
+    // The two key halves in turn, as their softmax warpgroups finish; a unit's first tile overwrites O once the
+    // epilogue has read the previous unit's (o_free).
+    if (lane == 0) {
+      const uint64_t vdesc0 = smem_desc(smem_addr(smem + V_OFF), BOX, 1024, kLayoutSw128);
+      int tile = 0, nunit = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
+        int b, h, qt;
+        unit_of(p, u, b, h, qt);
+        for (int kt = 0; kt <= qt; ++kt, ++tile) {
+          const int pb = tile & 1, pu = tile >> 1;
+          const int slot = tile % VS;
+          if (kt == 0 && nunit >= 1 && !wait(&o_free, (nunit - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          if (!wait(&v_full[slot], (tile / VS) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint64_t vd = vdesc0 + (uint64_t)(slot * (TILE >> 4));
+          const uint32_t pcol = tbase + COL_S + pb * 128;
+#pragma unroll
+          for (int x = 0; x < NWG; ++x) {
+            if (!wait(&p_full[x][pb], pu & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < KW / 16; ++kk)
+              mma_bf16_ts(tbase + COL_O, pcol + x * KW + kk * 8, vd + (uint64_t)((KW / 16 * x + kk) * 128), IDESC_O,
+                          (kt == 0 && x == 0 && kk == 0) ? 0u : 1u);
+          }
+          if (!ok) break;
+          tc_commit(&pv_done[pb]);
+          tc_commit(&v_empty[slot]);
+          OMNI_TRACE_AT(tile * 8 + 3);
+        }
+        if (ok) tc_commit(&o_ready);
+      }
+    }
+    __syncwarp();
+  } else if (warp < W_EPI) {
+    // ------------------------------------------------------------------ softmax, keys KW x .. of every tile
+    // The warpgroups leave their loops only on a decision taken at a barrier over all their threads, so that no
+    // thread waits at a barrier the others have left: a wait that gives up sets abort_flag and the thread goes on
+    // to the tile's barrier, where every thread sees it.
     const int x = warp >> 2;
     const int row = tid & 127;  // query row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const uint32_t col_o = tbase + lane_off + COL_O + x * 128;
+    const uint32_t col_o = tbase + lane_off + COL_O + x * DW;  // this warpgroup's head dims of O (rescale)
     int tile = 0, nunit = 0;
-    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
+    bool quit = false;
+    for (int u = blockIdx.x; u < units && !quit; u += gridDim.x, ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
       float m = -INFINITY, l = 0.f;
       for (int kt = 0; kt <= qt; ++kt, ++tile) {
         const int sb = tile & 1;
-        if (!wait(&s_full[sb], (tile >> 1) & 1)) break;
+        wait(&s_full[sb], (tile >> 1) & 1);
+        if (row == 0 && x < 2) OMNI_TRACE_AT(tile * 8 + 4 + 2 * x);
         tc_fence_after();
         __syncwarp();
-        const uint32_t scol = tbase + lane_off + COL_S + sb * 128 + x * 64;
-        uint32_t raw[64];
-        tmem_ld32_async(scol, raw);
-        tmem_ld32_async(scol + 32, raw + 32);
-        tmem_wait_ld();
-        float v[64];
+        const uint32_t scol = tbase + lane_off + COL_S + sb * 128 + x * KW;
+        uint32_t raw[KW];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(raw[i]);
+        for (int c = 0; c < KW / 32; ++c) tmem_ld32_async(scol + 32 * c, raw + 32 * c);
+        tmem_wait_ld();
+        if (row == 0 && x == 0 && tile < 400) OMNI_TRACE_AT(2400 + tile * 4);
+        float v[KW];
+#pragma unroll
+        for (int i = 0; i < KW; ++i) v[i] = __uint_as_float(raw[i]);
         if (kt == qt) {  // the diagonal tile: keys past the query
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (x * 64 + i > row) v[i] = -INFINITY;
+          for (int i = 0; i < KW; ++i)
+            if (x * KW + i > row) v[i] = -INFINITY;
         }
         float part[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) part[j] = v[j];
 #pragma unroll
-        for (int i = 8; i < 64; ++i) part[i & 7] = fmaxf(part[i & 7], v[i]);
+        for (int i = 8; i < KW; ++i) part[i & 7] = fmaxf(part[i & 7], v[i]);
         const float tmax = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
                                  fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7]))) * p.qscale;
-        // Raise the running max only when needed; then this half's O (built from earlier tiles) is rescaled. The
-        // probabilities are formed first, so that the scores are dead while O is rescaled (register pressure).
-        const float mnew = tmax > m + kRescale ? tmax : m;
-        const bool rescale = mnew != m && kt > 0;
-        const float mm = mnew == -INFINITY ? 0.f : mnew;  // a row with no key in this half yet: every p is 0
-        uint32_t w[32];
+        // One barrier per tile over the warpgroups: does any row need a higher max, or has any thread seen an abort?
+        const bool saw_abort = abort_flag != 0;
+        float mnew = m;
+        bool slow = false;
+        const bool any_raise = sync_or(1, SM_THREADS, tmax > m + kRescale || saw_abort);
+        if (row == 0 && x == 0 && tile < 400) OMNI_TRACE_AT(2401 + tile * 4);
+        if (any_raise) {
+          if (sync_or(1, SM_THREADS, saw_abort)) {
+            quit = true;
+            break;
+          }
+          ctl.tmax[x][row] = tmax;
+          named_sync(2, SM_THREADS);
+          float t2 = ctl.tmax[0][row];  // the same in every warpgroup
+#pragma unroll
+          for (int y = 1; y < NWG; ++y) t2 = fmaxf(t2, ctl.tmax[y][row]);
+          if (t2 > m + kRescale) mnew = t2;
+          slow = true;
+        }
+        // Probabilities (bf16 pairs) over this warpgroup's keys, and the row sum; formed before any rescale of O, so
+        // that the scores are dead by then (register pressure).
+        uint32_t w[KW / 2];
         float ls[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) ls[j] = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2(fmaf(v[2 * i], p.qscale, -mm));
-          const float p1 = ex2(fmaf(v[2 * i + 1], p.qscale, -mm));
+        for (int i = 0; i < KW / 2; ++i) {
+          const float p0 = ex2(fmaf(v[2 * i], p.qscale, -mnew));
+          const float p1 = ex2(fmaf(v[2 * i + 1], p.qscale, -mnew));
           ls[(2 * i) & 7] += p0;
           ls[(2 * i + 1) & 7] += p1;
           w[i] = pack_bf16x2(p0, p1);
         }
-        if (__any_sync(0xffffffffu, rescale)) {
-          if (!wait(&pv_done[x][(tile - 1) & 1], ((tile - 1) >> 1) & 1)) break;
-          tc_fence_after();
-          __syncwarp();
-          const float sc = rescale ? ex2(m - mnew) : 1.f;
+        if (slow) {
+          const bool rescale = mnew != m && kt > 0;
+          if (__any_sync(0xffffffffu, rescale)) {
+            wait(&pv_done[(tile - 1) & 1], ((tile - 1) >> 1) & 1);  // O holds every earlier tile
+            tc_fence_after();
+            __syncwarp();
+            const float sc = rescale ? ex2(m - mnew) : 1.f;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            uint32_t ow[32];
-            tmem_ld32(col_o + c * 32, o);
+            for (int c = 0; c < DW / 32; ++c) {
+              float o[32];
+              uint32_t ow[32];
+              tmem_ld32(col_o + c * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(o[i] * sc);
-            tmem_st32(col_o + c * 32, ow);
+              for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(o[i] * sc);
+              tmem_st32(col_o + c * 32, ow);
+            }
+            tmem_wait_st();
+            l *= sc;
           }
-          tmem_wait_st();
-          l *= sc;
+          m = mnew;
         }
-        m = mnew;
         l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-        tmem_st32(scol, w);  // over this half's scores, which are in registers already
+        if (row == 0 && x == 0 && tile < 400) OMNI_TRACE_AT(2402 + tile * 4);
+        // P over this warpgroup's scores, which are in registers already.
+        if constexpr (KW / 2 == 32) tmem_st32(scol, w);
+        else tmem_st16(scol, w);
         tmem_wait_st();
+        if (row == 0 && x == 0 && tile < 400) OMNI_TRACE_AT(2403 + tile * 4);
         tc_fence_before();
         mbar_arrive(&p_full[x][sb]);
+        if (row == 0 && x < 2) OMNI_TRACE_AT(tile * 8 + 5 + 2 * x);
       }
-      if (abort_flag) break;
-      // The unit's (max, sum) of this half for the epilogue, once the epilogue has read the previous unit's: a unit
-      // of one or two tiles can be finished before that, and ml_full must not complete two phases ahead of its
-      // waiter.
-      if (nunit >= 1 && !wait(&ml_free, (nunit - 1) & 1)) break;
-      ml_stash[x][row] = make_float2(m, l);
-      mbar_arrive(&ml_full);
+      if (quit) break;
+      // The unit's row sums of these keys for the epilogue, once it has read the previous unit's (a unit of one or
+      // two tiles can be finished before that, and l_full must not complete two phases ahead of its waiter).
+      if (nunit >= 1) wait(&l_free, (nunit - 1) & 1);
+      ctl.lsum[x][row] = l;
+      mbar_arrive(&l_full);
     }
-  } else if (warp < 12) {
-    // ------------------------------------------------------------------ epilogue (thread = query row)
+  } else if (warp < W_EPI + 4) {
+    // ------------------------------------------------------------------ Q loader and epilogue (thread = query row)
     const int row = tid & 127;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    // Query rows of unit u (thread = row; rows past the width are zeros) into TMEM Q buffer j, as bf16 pairs.
+    auto load_q = [&](int u, int j) {
+      int b, h, qt;
+      unit_of(p, u, b, h, qt);
+      const int w = qt * BM + row;
+      const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_sb + (int64_t)h * p.q_sh +
+                                                        (int64_t)w * p.q_sw);
+      const uint32_t qcol = tbase + lane_off + COL_Q + j * 64;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // 64 head dims (32 columns of bf16 pairs) at a time
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 t = w < p.width ? __ldg(src + 8 * half + i) : make_uint4(0u, 0u, 0u, 0u);
+          r[4 * i] = t.x;
+          r[4 * i + 1] = t.y;
+          r[4 * i + 2] = t.z;
+          r[4 * i + 3] = t.w;
+        }
+        tmem_st32(qcol + 32 * half, r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&q_full[j]);
+    };
+    load_q(blockIdx.x, 0);
     int nunit = 0;
     for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
+      if (u + (int)gridDim.x < units) {  // the next unit's queries, once its buffer's last S has completed
+        const int n1 = nunit + 1;
+        if (n1 >= 2 && !wait(&q_free[n1 & 1], ((n1 >> 1) - 1) & 1)) break;
+        tc_fence_after();
+        load_q(u + gridDim.x, n1 & 1);
+      }
       if (!wait(&o_ready, nunit & 1)) break;
-      if (!wait(&ml_full, nunit & 1)) break;
+      if (!wait(&l_full, nunit & 1)) break;
+      if (row == 0) OMNI_TRACE_AT(1600 + nunit * 2);
       tc_fence_after();
       __syncwarp();
-      const float2 e0 = ml_stash[0][row], e1 = ml_stash[1][row];
-      mbar_arrive(&ml_free);
-      const float mx = fmaxf(e0.x, e1.x);
-      const float a0 = e0.y > 0.f ? ex2(e0.x - mx) : 0.f;
-      const float a1 = e1.y > 0.f ? ex2(e1.x - mx) : 0.f;
-      const float den = e0.y * a0 + e1.y * a1;
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      const float f0 = a0 * inv, f1 = a1 * inv;
+      float l = 0.f;
+#pragma unroll
+      for (int y = 0; y < NWG; ++y) l += ctl.lsum[y][row];
+      mbar_arrive(&l_free);
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       const int q = qt * BM + row;
       __nv_bfloat16* dst = p.out + (int64_t)b * p.out_sb + (int64_t)q * p.out_sw + (int64_t)h * p.out_sh;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t r0[32], r1[32];
+        uint32_t r0[32];
         tmem_ld32_async(tbase + lane_off + COL_O + c * 32, r0);
-        tmem_ld32_async(tbase + lane_off + COL_O + 128 + c * 32, r1);
         tmem_wait_ld();
         if (q < p.width) {
 #pragma unroll
@@ -442,9 +528,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const int k = 8 * i + 2 * j;
-              const float lo = fmaf(__uint_as_float(r0[k]), f0, __uint_as_float(r1[k]) * f1);
-              const float hi = fmaf(__uint_as_float(r0[k + 1]), f0, __uint_as_float(r1[k + 1]) * f1);
-              w4[j] = pack_bf16x2(lo, hi);
+              w4[j] = pack_bf16x2(__uint_as_float(r0[k]) * inv, __uint_as_float(r0[k + 1]) * inv);
             }
             *reinterpret_cast<uint4*>(dst + c * 32 + i * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
@@ -452,20 +536,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(&o_free);
+      if (row == 0) OMNI_TRACE_AT(1601 + nunit * 2);
     }
   }
   __syncthreads();
   if (abort_flag) {
     if (tid == 0) raise_status(p.status, kStatusTimeout);
-    if (tid == W_MMA * 32) {
-      tc_commit(&drain);  // every MMA the issuer thread issued has completed once this arrives
+    if (tid == W_MMA * 32 || tid == W_MMA_PV * 32) {
+      // Every MMA an issuer thread issued has completed once its commit arrives (two issuers: two arrivals).
+      tc_commit(&drain);
       mbar_wait(&drain, 0);
     }
     if (tid == W_LOADK * 32) {
       // Let the latest load of every slot land (a slot is refilled only after its previous load was consumed).
       for (int i = issued_k > KS ? issued_k - KS : 0; i < issued_k; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1);
       for (int i = issued_v > VS ? issued_v - VS : 0; i < issued_v; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1);
-      for (int i = issued_q > QS ? issued_q - QS : 0; i < issued_q; ++i) mbar_wait(&q_full[i % QS], (i / QS) & 1);
     }
   }
   tc_fence_before();
@@ -474,6 +559,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }
+  OMNI_TRACE_CTA(1);
 }
 
 // (row, head) pairs per scheduling group: about 16, so that one group's units cover the grid once or twice and its
@@ -511,9 +597,8 @@ bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t 
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   using namespace prefill;
-  CUtensorMap qm, km, vm;
-  if (!make_map(&qm, a.q, a.batch, a.heads, a.width, a.q_sb, a.q_sh, a.q_sw) ||
-      !make_map(&km, a.k, a.batch, a.heads, a.width, a.k_sb, a.k_sh, a.k_sw) ||
+  CUtensorMap km, vm;
+  if (!make_map(&km, a.k, a.batch, a.heads, a.width, a.k_sb, a.k_sh, a.k_sw) ||
       !make_map(&vm, a.v, a.batch, a.heads, a.width, a.v_sb, a.v_sh, a.v_sw))
     return cudaErrorInvalidValue;
   static bool configured = false;
@@ -529,6 +614,10 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.qtiles = (a.width + BM - 1) / BM;
   p.qscale = a.scale * kLog2e;
   p.group = prefill_group(a.batch * a.heads);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  p.q_sb = a.q_sb;
+  p.q_sh = a.q_sh;
+  p.q_sw = a.q_sw;
   p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
   p.out_sb = a.o_sb;
   p.out_sw = a.o_sw;
@@ -538,7 +627,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   int grid = device_sm_count();
   if (grid > units) grid = units;
   if (grid <= 0) return cudaSuccess;
-  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p);
+  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, km, vm, p);
 }
 
 }  // namespace omni
