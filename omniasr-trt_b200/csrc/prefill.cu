@@ -7,20 +7,23 @@
 //
 // Work unit: (row b, head h, 128-query tile qt) over key tiles 0..qt; units are taken by a persistent grid of one
 // CTA per SM in groups of (b, h) pairs, heaviest first within a group (unit_of). Roles (512 threads):
-//   warp 12 TMA: the K tiles (3-slot ring, two 64-column boxes each, 128-byte swizzle); warp 14 TMA: the V tiles
-//   warp 13 MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys, double-buffered) with Q read from TMEM (the
-//           tcgen05 "A in TMEM" form); warp 15 MMA: O += P V with P read from TMEM as well. Two issuing threads,
-//           because one thread issues a tcgen05.mma in about 55 clocks at best (measured), while a 128x128x16 MMA
-//           takes the tensor core about 64: a single issuer with its waits left the tensor core idle half the time.
-//           Only K and V come from shared memory.
+//   warp 12 TMA: the K tiles (3-slot ring, two 64-column boxes each, 128-byte swizzle); warp 14 TMA: the V tiles;
+//           the query tiles (2 slots) are loaded two units ahead by the first epilogue thread
+//   warp 13 MMA: S = Q K^T into TMEM (M=128 queries, N=128 keys), triple-buffered, so that S(t + 3) needs only
+//           O += P(t) V to have completed and the scores are ready before the softmax asks for them;
+//   warp 15 MMA: O += P V with P read from TMEM (the tcgen05 "A in TMEM" form). Two issuing threads, because one
+//           thread issues a tcgen05.mma in about 55 clocks at best (measured), while a 128x128x16 MMA takes the
+//           tensor core about 64: a single issuer with its waits left the tensor core idle half the time.
 //   warps 0-3 / 4-7  softmax warpgroups x = 0 / 1: thread t of warpgroup x owns query row t and the keys 64x .. 64x+63
 //           of every tile, so twice the softmax warps per SM each form half a tile's exponentials. The two keep one
 //           running max per row: each tile one barrier over both warpgroups asks whether any row's scores pass its
 //           max by 2^8 (log2 units); only then are the tile maxima exchanged, the max raised and O rescaled in TMEM
 //           (each warpgroup its 64 head dims). P (bf16 pairs) is written over the warpgroup's half of S in TMEM.
-//   warps 8-11 Q loader and epilogue: per unit, the next unit's query rows into TMEM (thread t = row t), then
-//           O / (l_0 + l_1) of this unit as bf16 rows, while the softmax warpgroups go on with the next unit.
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) Q0 [384,448) Q1 [448,512); P of S buffer j, half x at 128j + 64x .. +32.
+//           The scale-and-subtract and the row sums use the packed f32x2 FMA / add (two elements per instruction),
+//           and one probability pair in four is exponentiated on the FMA pipe (ex2_fma) instead of the
+//           special-function unit, which the exponentials otherwise saturate.
+//   warps 8-11 epilogue: O / (l_0 + l_1) of each unit as bf16 rows, while the softmax warpgroups go on with the next.
+// TMEM: S0 [0,128) S1 [128,256) S2 [256,384) O [384,512); P of S buffer j, half x at 128j + 64x .. +32.
 
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -38,10 +41,12 @@ constexpr int BM = 128;  // queries per tile
 constexpr int BN = 128;  // keys per tile
 constexpr int TILE = BN * D * 2;
 constexpr int BOX = BN * 64 * 2;
-constexpr int KS = 3, VS = 3;
-constexpr int K_OFF = 0;
+constexpr int QS = 2, KS = 3, VS = 2;  // query tiles (two units), K and V rings, in shared memory
+constexpr int Q_OFF = 0;
+constexpr int K_OFF = Q_OFF + QS * TILE;
 constexpr int V_OFF = K_OFF + KS * TILE;
 constexpr int SMEM_BYTES = V_OFF + VS * TILE;
+constexpr int NSB = 3;  // S buffers in TMEM: S(t + 3) needs only O += P(t) V to have completed
 constexpr int NWG = 2;        // softmax warpgroups; warpgroup x owns keys KW x .. KW x + KW - 1 of every tile
 constexpr int KW = BN / NWG;  // keys per softmax warpgroup (a multiple of the 16-key MMA step)
 constexpr int DW = D / NWG;   // head dims of O each softmax warpgroup rescales
@@ -49,10 +54,14 @@ constexpr int W_EPI = 4 * NWG, W_LOADK = W_EPI + 4, W_MMA = W_LOADK + 1, W_LOADV
 constexpr int THREADS = 32 * (W_MMA_PV + 1);  // softmax, Q loader + epilogue, K loads, S MMAs, V loads, PV MMAs
 constexpr int SM_THREADS = 128 * NWG;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_Q = 384;  // S buffer j at 128 j; Q buffer j at 384 + 64 j
+constexpr uint32_t COL_S = 0, COL_O = 384;  // S buffer j at 128 j
 constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(BM, D, 0, 1);
 constexpr float kRescale = 8.f;
+#ifndef OMNI_PREFILL_POLY_EVERY
+#define OMNI_PREFILL_POLY_EVERY 4
+#endif
+constexpr int kPolyEvery = OMNI_PREFILL_POLY_EVERY;  // probabilities of one pair in this many by ex2_fma
 
 struct Params {
   int batch, heads, width, qtiles;
@@ -104,6 +113,43 @@ OMNI_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 
+// 2^x on the FMA and integer pipes, for x <= 127 (the softmax's arguments are at most 8): x = j + f with j the
+// nearest integer (the 1.5 * 2^23 addition leaves j in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f from a
+// cubic fitted here for relative error on [-0.5, 0.5] (7.5e-5 at most, far below bf16's 2^-9); 2^j added to the
+// exponent field. x is clamped to -126 (2^-126 or a denormal below it: zero to a probability), so that the exponent
+// field never wraps. Used for part of the probabilities, so that the special-function unit, which forms the others
+// with ex2, is not the only pipe the exponentials load.
+OMNI_DEV float ex2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float q = fmaf(fmaf(fmaf(0.055174146f, f, 0.24261758f), f, 0.69326109f), f, 0.99992758f);
+  return __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
+}
+
+// Packed pairs of floats for the f32x2 forms of fma / add (one instruction for two elements on the FMA pipe).
+OMNI_DEV uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+OMNI_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+OMNI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+OMNI_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+OMNI_DEV float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Two floats rounded to bf16 and packed (lo in the low half).
 OMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
@@ -153,14 +199,15 @@ OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
 // for the epilogue, flags. One static struct, padded to 1024 bytes, so that the dynamic tile ring after it starts
 // 1024-aligned (the kernel checks, and reports status bit 4 otherwise).
 struct alignas(1024) Ctl {
-  uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], q_full[2], q_free[2];
-  uint64_t s_full[2], p_full[NWG][2], pv_done[2], o_ready, o_free, l_full, l_free, drain;
+  uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], q_full[QS], q_empty[QS];
+  uint64_t s_full[NSB], p_full[NWG][NSB], pv_done[NSB], o_ready, o_free, l_full, l_free, drain;
   float tmax[NWG][BM];  // [warpgroup][row]: a tile's scaled row maxima, on the rare tiles that raise a max
   float lsum[NWG][BM];  // [warpgroup][row]: the unit's row sums for the epilogue
   uint32_t tmem_base;
-  int abort_flag, issued_k, issued_v;  // loads the producers issued
+  int abort_flag, issued_k, issued_v, issued_q;  // loads the producers issued
 };
 static_assert(sizeof(Ctl) + SMEM_BYTES <= 232448, "shared memory per block");
+static_assert(NSB * 128 + D <= TMEM_COLS, "S buffers and O in TMEM");
 
 OMNI_DEV bool sync_or(int id, int count, bool pred) {
   uint32_t out;
@@ -176,17 +223,17 @@ OMNI_DEV bool sync_or(int id, int count, bool pred) {
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const Params p) {
+    prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const Params p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ Ctl ctl;
   uint64_t *k_full = ctl.k_full, *k_empty = ctl.k_empty, *v_full = ctl.v_full, *v_empty = ctl.v_empty;
-  uint64_t *q_full = ctl.q_full, *q_free = ctl.q_free, *s_full = ctl.s_full, *pv_done = ctl.pv_done;
-  uint64_t(*p_full)[2] = ctl.p_full;
+  uint64_t *q_full = ctl.q_full, *q_empty = ctl.q_empty, *s_full = ctl.s_full, *pv_done = ctl.pv_done;
+  uint64_t(*p_full)[NSB] = ctl.p_full;
   uint64_t &o_ready = ctl.o_ready, &o_free = ctl.o_free, &l_full = ctl.l_full, &l_free = ctl.l_free;
   uint64_t& drain = ctl.drain;
   volatile int& abort_flag = ctl.abort_flag;
-  volatile int &issued_k = ctl.issued_k, &issued_v = ctl.issued_v;
+  volatile int &issued_k = ctl.issued_k, &issued_v = ctl.issued_v, &issued_q = ctl.issued_q;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -207,9 +254,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int j = 0; j < 2; ++j) {
-      mbar_init(&q_full[j], 128);
-      mbar_init(&q_free[j], 1);
+    for (int j = 0; j < QS; ++j) {
+      mbar_init(&q_full[j], 1);
+      mbar_init(&q_empty[j], 1);
+    }
+    for (int j = 0; j < NSB; ++j) {
       mbar_init(&s_full[j], 1);
       mbar_init(&pv_done[j], 1);
       for (int x = 0; x < NWG; ++x) mbar_init(&p_full[x][j], 128);
@@ -221,7 +270,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&drain, 2);
     mbar_fence_init();
     abort_flag = 0;
-    issued_k = issued_v = 0;
+    issued_k = issued_v = issued_q = 0;
   }
   if (warp == W_EPI) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
   tc_fence_before();
@@ -266,23 +315,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp == W_MMA) {
-    // ------------------------------------------------------------------ S issuer: S[t & 1] = Q K(t)^T
-    // S[t & 1] is free once O += P(t - 2) V has completed (P(t - 2) lies over it); its own Q buffer stays until the
-    // unit's last S has completed (q_free).
+    // ------------------------------------------------------------------ S issuer: S[t % NSB] = Q K(t)^T
+    // S[t % NSB] is free once O += P(t - NSB) V has completed (P(t - NSB) lies over it); the unit's Q slot is
+    // released after its last S (q_empty).
     if (lane == 0) {
       // Slot s's descriptor is slot 0's with the start address (in 16-byte units, 14 bits) moved on by s tiles.
       const uint64_t kdesc0 = smem_desc(smem_addr(smem + K_OFF), 16, 1024, kLayoutSw128);
-      int tile = 0, nunit = 0;
+      const uint64_t qdesc0 = smem_desc(smem_addr(smem + Q_OFF), 16, 1024, kLayoutSw128);
+      int tile = 0, nunit = 0, sb = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
-        const int qb = nunit & 1;
-        if (!wait(&q_full[qb], (nunit >> 1) & 1)) break;
-        const uint32_t qcol = tbase + COL_Q + qb * 64;
-        for (int kt = 0; kt <= qt; ++kt, ++tile) {
+        const int qslot = nunit % QS;
+        if (!wait(&q_full[qslot], (nunit / QS) & 1)) break;
+        const uint64_t qd = qdesc0 + (uint64_t)(qslot * (TILE >> 4));
+        for (int kt = 0; kt <= qt; ++kt, ++tile, sb = sb == NSB - 1 ? 0 : sb + 1) {
           const int slot = tile % KS;
-          if (tile >= 2 && !wait(&pv_done[tile & 1], ((tile - 2) >> 1) & 1)) {
+          if (tile >= NSB && !wait(&pv_done[sb], ((tile - NSB) / NSB) & 1)) {
             ok = false;
             break;
           }
@@ -291,15 +341,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t dcol = tbase + COL_S + (tile & 1) * 128;
+          const uint32_t dcol = tbase + COL_S + sb * 128;
           const uint64_t kd = kdesc0 + (uint64_t)(slot * (TILE >> 4));
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_bf16_ts(dcol, qcol + kk * 8, kd + (uint64_t)((((kk >> 2) * BOX + (kk & 3) * 32) >> 4)), IDESC_S,
-                        kk > 0 ? 1u : 0u);
-          tc_commit(&s_full[tile & 1]);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t off = (uint64_t)((((kk >> 2) * BOX + (kk & 3) * 32) >> 4));
+            mma_bf16_ss(dcol, qd + off, kd + off, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[sb]);
           tc_commit(&k_empty[slot]);
-          if (kt == qt) tc_commit(&q_free[qb]);  // the unit's last read of its Q buffer
+          if (kt == qt) tc_commit(&q_empty[qslot]);  // the unit's last read of its query tile
           OMNI_TRACE_AT(tile * 8 + 2);
         }
       }
@@ -317,7 +368,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         int b, h, qt;
         unit_of(p, u, b, h, qt);
         for (int kt = 0; kt <= qt; ++kt, ++tile) {
-          const int pb = tile & 1, pu = tile >> 1;
+          const int pb = tile % NSB, pu = tile / NSB;
           const int slot = tile % VS;
           if (kt == 0 && nunit >= 1 && !wait(&o_free, (nunit - 1) & 1)) {
             ok = false;
@@ -366,8 +417,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       unit_of(p, u, b, h, qt);
       float m = -INFINITY, l = 0.f;
       for (int kt = 0; kt <= qt; ++kt, ++tile) {
-        const int sb = tile & 1;
-        wait(&s_full[sb], (tile >> 1) & 1);
+        const int sb = tile % NSB;
+        if (row == 0 && x == 0 && tile < 300) OMNI_TRACE_AT(2400 + 1200 + tile);
+        wait(&s_full[sb], (tile / NSB) & 1);
         if (row == 0 && x < 2) OMNI_TRACE_AT(tile * 8 + 4 + 2 * x);
         tc_fence_after();
         __syncwarp();
@@ -385,13 +437,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < KW; ++i)
             if (x * KW + i > row) v[i] = -INFINITY;
         }
+        static_assert(KW % 16 == 0, "row max in 8 partials of two values per step");
         float part[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) part[j] = v[j];
 #pragma unroll
-        for (int i = 8; i < KW; ++i) part[i & 7] = fmaxf(part[i & 7], v[i]);
-        const float tmax = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
-                                 fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7]))) * p.qscale;
+        for (int i = 8; i < KW; i += 16)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) part[j] = max3(part[j], v[i + j], v[i + 8 + j]);
+        const float tmax = max3(max3(part[0], part[1], part[2]), max3(part[3], part[4], part[5]),
+                                fmaxf(part[6], part[7])) * p.qscale;
         // One barrier per tile over the warpgroups: does any row need a higher max, or has any thread seen an abort?
         const bool saw_abort = abort_flag != 0;
         float mnew = m;
@@ -414,21 +469,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Probabilities (bf16 pairs) over this warpgroup's keys, and the row sum; formed before any rescale of O, so
         // that the scores are dead by then (register pressure).
         uint32_t w[KW / 2];
-        float ls[8];
+        uint64_t ls2[4];  // row-sum partials, two per packed register
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ls[j] = 0.f;
+        for (int j = 0; j < 4; ++j) ls2[j] = 0ull;
+        const uint64_t sc2 = f2_pack(p.qscale, p.qscale), nm2 = f2_pack(-mnew, -mnew);
 #pragma unroll
         for (int i = 0; i < KW / 2; ++i) {
-          const float p0 = ex2(fmaf(v[2 * i], p.qscale, -mnew));
-          const float p1 = ex2(fmaf(v[2 * i + 1], p.qscale, -mnew));
-          ls[(2 * i) & 7] += p0;
-          ls[(2 * i + 1) & 7] += p1;
+          // x = s * scale - max for a pair in one packed FMA; one pair in kPolyEvery exponentiated on the FMA pipe,
+          // the rest on the special-function unit.
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sc2, nm2), x0, x1);
+          const bool poly = i % kPolyEvery == kPolyEvery - 1;
+          const float p0 = poly ? ex2_fma(x0) : ex2(x0);
+          const float p1 = poly ? ex2_fma(x1) : ex2(x1);
+          ls2[i & 3] = f2_add(ls2[i & 3], f2_pack(p0, p1));
           w[i] = pack_bf16x2(p0, p1);
         }
+        float ls[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f2_unpack(ls2[j], ls[2 * j], ls[2 * j + 1]);
         if (slow) {
           const bool rescale = mnew != m && kt > 0;
           if (__any_sync(0xffffffffu, rescale)) {
-            wait(&pv_done[(tile - 1) & 1], ((tile - 1) >> 1) & 1);  // O holds every earlier tile
+            wait(&pv_done[(tile - 1) % NSB], ((tile - 1) / NSB) & 1);  // O holds every earlier tile
             tc_fence_after();
             __syncwarp();
             const float sc = rescale ? ex2(m - mnew) : 1.f;
@@ -465,44 +528,32 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&l_full);
     }
   } else if (warp < W_EPI + 4) {
-    // ------------------------------------------------------------------ Q loader and epilogue (thread = query row)
+    // ------------------------------------------------------------------ epilogue (thread = query row)
     const int row = tid & 127;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    // Query rows of unit u (thread = row; rows past the width are zeros) into TMEM Q buffer j, as bf16 pairs.
-    auto load_q = [&](int u, int j) {
+    // One thread also loads the query tiles, two units ahead: unit n + 2's goes into unit n's slot once unit n's last
+    // S has completed (q_empty, before its O is ready), so a unit's first S never waits for its queries.
+    const bool q_loader = tid == W_EPI * 32;
+    auto load_q = [&](int n, int u) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
-      const int w = qt * BM + row;
-      const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_sb + (int64_t)h * p.q_sh +
-                                                        (int64_t)w * p.q_sw);
-      const uint32_t qcol = tbase + lane_off + COL_Q + j * 64;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {  // 64 head dims (32 columns of bf16 pairs) at a time
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 t = w < p.width ? __ldg(src + 8 * half + i) : make_uint4(0u, 0u, 0u, 0u);
-          r[4 * i] = t.x;
-          r[4 * i + 1] = t.y;
-          r[4 * i + 2] = t.z;
-          r[4 * i + 3] = t.w;
-        }
-        tmem_st32(qcol + 32 * half, r);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&q_full[j]);
+      const int qslot = n % QS;
+      mbar_arrive_expect_tx(&q_full[qslot], TILE);
+      tma_load_4d(smem + Q_OFF + qslot * TILE, &qmap, 0, qt * BM, h, b, &q_full[qslot]);
+      tma_load_4d(smem + Q_OFF + qslot * TILE + BOX, &qmap, 64, qt * BM, h, b, &q_full[qslot]);
+      issued_q = n + 1;
     };
-    load_q(blockIdx.x, 0);
+    if (q_loader) {
+      prefetch_tmap(&qmap);
+      for (int n = 0; n < QS && (int)blockIdx.x + n * (int)gridDim.x < units; ++n) load_q(n, blockIdx.x + n * gridDim.x);
+    }
     int nunit = 0;
     for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
-      if (u + (int)gridDim.x < units) {  // the next unit's queries, once its buffer's last S has completed
-        const int n1 = nunit + 1;
-        if (n1 >= 2 && !wait(&q_free[n1 & 1], ((n1 >> 1) - 1) & 1)) break;
-        tc_fence_after();
-        load_q(u + gridDim.x, n1 & 1);
+      if (q_loader && u + QS * (int)gridDim.x < units) {
+        if (!wait(&q_empty[nunit % QS], (nunit / QS) & 1)) break;
+        load_q(nunit + QS, u + QS * gridDim.x);
       }
       if (!wait(&o_ready, nunit & 1)) break;
       if (!wait(&l_full, nunit & 1)) break;
@@ -551,6 +602,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Let the latest load of every slot land (a slot is refilled only after its previous load was consumed).
       for (int i = issued_k > KS ? issued_k - KS : 0; i < issued_k; ++i) mbar_wait(&k_full[i % KS], (i / KS) & 1);
       for (int i = issued_v > VS ? issued_v - VS : 0; i < issued_v; ++i) mbar_wait(&v_full[i % VS], (i / VS) & 1);
+      for (int i = issued_q > QS ? issued_q - QS : 0; i < issued_q; ++i) mbar_wait(&q_full[i % QS], (i / QS) & 1);
     }
   }
   tc_fence_before();
@@ -597,8 +649,9 @@ bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t 
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   using namespace prefill;
-  CUtensorMap km, vm;
-  if (!make_map(&km, a.k, a.batch, a.heads, a.width, a.k_sb, a.k_sh, a.k_sw) ||
+  CUtensorMap qm, km, vm;
+  if (!make_map(&qm, a.q, a.batch, a.heads, a.width, a.q_sb, a.q_sh, a.q_sw) ||
+      !make_map(&km, a.k, a.batch, a.heads, a.width, a.k_sb, a.k_sh, a.k_sw) ||
       !make_map(&vm, a.v, a.batch, a.heads, a.width, a.v_sb, a.v_sh, a.v_sw))
     return cudaErrorInvalidValue;
   static bool configured = false;
@@ -627,7 +680,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   int grid = device_sm_count();
   if (grid > units) grid = units;
   if (grid <= 0) return cudaSuccess;
-  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, km, vm, p);
+  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p);
 }
 
 }  // namespace omni
