@@ -910,7 +910,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     value = world * wl.step_units / (ms_step * 1e-3) / scale
     achieved = wl.roof_units / (roof_ms * 1e-3) / scale
     line = {
-        "metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+        "metric": wl.metric + ("" if (H, D) == (32, 128) else f" [{H} heads x {D}]"), "value": round(value, 1),
+        "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": "strong" if args.workload == "sweep" else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 tensors; lengths and parents from the seed-0 CPU generator)",
@@ -1205,7 +1206,14 @@ def main():
     p.add_argument("--tokens-out", default=None, help="step workload: save the generated tokens (.npy)")
     p.add_argument("--decode-steps", type=int, default=STEP_STEPS, help="step workload: decoder steps per run")
     p.add_argument("--dtype", choices=["bf16", "f32"], default="bf16", help="step workload: model dtype")
+    p.add_argument("--heads", type=int, default=H, help="attention workloads: heads (heads x head_dim = 4096)")
+    p.add_argument("--head-dim", type=int, default=D,
+                   help="attention workloads: head_dim; 512 with 8 heads is the shipped model's geometry")
     args = p.parse_args()
+    global H, D
+    if args.heads * args.head_dim != H * D:
+        p.error(f"heads x head_dim must be {H * D} (the decoder's model width)")
+    H, D = args.heads, args.head_dim
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
