@@ -1195,6 +1195,7 @@ def run_reference(args, rank: int) -> dict | None:
 
 
 def main():
+    global H, D
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
@@ -1210,7 +1211,6 @@ def main():
     p.add_argument("--head-dim", type=int, default=D,
                    help="attention workloads: head_dim; 512 with 8 heads is the shipped model's geometry")
     args = p.parse_args()
-    global H, D
     if args.heads * args.head_dim != H * D:
         p.error(f"heads x head_dim must be {H * D} (the decoder's model width)")
     H, D = args.heads, args.head_dim
