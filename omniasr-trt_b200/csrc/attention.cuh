@@ -57,20 +57,22 @@ cudaError_t launch_split(int dtype, int dim, bool gather, const SplitPlan& plan,
 cudaError_t launch_combine(int dtype, int dim, const float* part_o, const float* part_ml, void* out,
                            int64_t rows_heads, int st, cudaStream_t stream);
 
-// Tensor-core pass (bf16, head_dim 128, 1..16 queries per group): persistent stream-K split, see attention_tc.cu.
+// Tensor-core pass (bf16, head_dim 128 or 512, 1..16 queries per group): persistent stream-K split, see
+// attention_tc.cu.
 struct TcParams {
-  const __nv_bfloat16* q;  // [groups * nq, heads, 128]
+  const __nv_bfloat16* q;  // [groups * nq, heads, dim]
   const int64_t* lengths;  // [groups]
   int groups, nq, causal, heads;
+  int dim;        // head_dim: 128 or 512
   int64_t cap;    // min(cache length, keys): keys a unit may read (set by launch_tc_pass)
   float qscale;   // softmax scale * log2(e)
-  float* part_o;  // [groups * nq, heads, st, 128]
+  float* part_o;  // [groups * nq, heads, st, dim]
   float* part_ml; // [groups * nq, heads, st, 2]
   int st;         // segments per (row, head) (set by launch_tc_pass)
   int grid;       // CTAs of the pass (set by launch_tc_pass)
   int unit_cost;  // scheduling cost of a unit's start, in eighths of a tile (set by launch_tc_pass)
   int prefetch;   // tiles prefetched into L2 ahead of the loads (set by launch_tc_pass)
-  __nv_bfloat16* out;  // [groups * nq, heads, 128]: units a single CTA finishes are written here directly
+  __nv_bfloat16* out;  // [groups * nq, heads, dim]: units a single CTA finishes are written here directly
                        // (null: every unit goes through the combine, e.g. when a second pass adds partials)
   unsigned* counters;  // [groups * heads] segments published per unit, zero on entry and left zero; non-null (with
                        // out): the last CTA to finish a unit merges its segments itself and no combine runs
@@ -87,7 +89,7 @@ int tc_segments(int64_t keys);
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream);
 // Beam search's generated keys, attended inside the combine (before it waits for the pass): row r's key j < gen_len[r]
-// comes from cache row ptr[r, j] at position j (bf16, head_dim 128).
+// comes from cache row ptr[r, j] at position j (bf16, head_dim as the pass's).
 struct GenKeys {
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;

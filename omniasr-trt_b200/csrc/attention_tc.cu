@@ -43,18 +43,23 @@ constexpr int BOX_BYTES = BN * 64 * 2;  // one 64-column box of a tile
 
 // Shared-memory layout of a CTA with SLOTS tile slots: K of tile i in slot i % (SLOTS / 2), V in slot
 // SLOTS / 2 + i % (SLOTS / 2), so K loads never wait behind V loads (each has its own producer).
-template <int SLOTS>
+template <int SLOTS, int DIM>
 struct Smem {
-  static constexpr int Q_OFF = SLOTS * SLOT_BYTES;      // two query buffers (units u and u + 1), 4 KB each
-  static constexpr int P_OFF = Q_OFF + 2 * NQP * D * 2;
+  static constexpr int Q_OFF = SLOTS * SLOT_BYTES;      // two query buffers (units u and u + 1), NQP x DIM each
+  static constexpr int P_OFF = Q_OFF + 2 * NQP * DIM * 2;
   static constexpr int RED_OFF = P_OFF + 2 * NQP * BN * 2;         // column maxima of the 4 softmax warps
   static constexpr int RED_L_OFF = RED_OFF + 4 * NQP * 4;           // column sums of a finished unit
   static constexpr int STASH_M_OFF = RED_L_OFF + 4 * NQP * 4;       // its running max per column
-  static constexpr int STASH_OFF = STASH_M_OFF + NQP * 4;           // its accumulator [NQP][128 dims]
-  static constexpr int BYTES = STASH_OFF + NQP * D * 4 + 1024;      // + alignment slack
+  static constexpr int STASH_OFF = STASH_M_OFF + NQP * 4;           // its accumulator [NQP][DIM dims]
+  static constexpr int BYTES = STASH_OFF + NQP * DIM * 4 + 1024;    // + alignment slack
 };
-constexpr int THREADS = 256;  // warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads, 7 write-out
-constexpr uint32_t TMEM_COLS = 64;  // S^T x2 (cols 0-31), O^T x2 (cols 32-63)
+// Warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads, 7 write-out; with head_dim 512 also warp 8, which
+// zeroes the V rows past a unit's keys in its last tile (the key tile's four 128-dim chunks stream through the ring,
+// so the softmax warps, which did this for head_dim 128, cannot wait for all of them).
+constexpr int threads_for(int dim) { return dim == 128 ? 256 : 288; }
+// TMEM: S^T x2 (cols 0-31), then O^T x2 per 128-dim chunk of the head (16 columns each).
+constexpr uint32_t tmem_cols(int dim) { return dim == 128 ? 64u : 256u; }
+OMNI_DEV uint32_t ocol(int buf, int chunk, int dc) { return 2 * NQP + (buf * dc + chunk) * NQP; }
 constexpr uint32_t IDESC_S = idesc_bf16(128, NQP, 0, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(128, NQP, 1, 1);
 
@@ -249,40 +254,48 @@ OMNI_DEV void store_out4(__nv_bfloat16* dst, const float4& a, float inv) {
 }
 
 // Output rows of unit (g, h) from its nseg segments: segment `own` from this CTA's stash, the others' from the
-// partial arrays (read through L2: other CTAs wrote them). One warp; lane l holds dims 4l .. 4l+3. Segments go
-// outermost so that a chunk of queries has all its loads of one segment in flight at once; the merge is the
-// combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max), segments that saw no key take no part.
-template <int NQT>
+// partial arrays (read through L2: other CTAs wrote them). One warp; lane l holds dims 4l .. 4l+3 of each 128-dim
+// chunk of the head. Segments go outermost so that a chunk of queries has all its loads of one segment in flight at
+// once; the merge is the combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max), segments that saw no
+// key take no part.
+template <int NQT, int DIM>
 OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int lane, const float* red_l,
                          const float* stash_m, const float* stash) {
-  constexpr int JC = NQT < 8 ? NQT : 8;  // queries per chunk (register budget)
+  constexpr int DC = DIM / D;
+  constexpr int JC = (NQT < 8 ? NQT : 8) / DC > 0 ? (NQT < 8 ? NQT : 8) / DC : 1;  // queries per chunk (registers)
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
 #pragma unroll 1
   for (int j0 = 0; j0 < NQT && j0 < p.nq; j0 += JC) {
     float m[JC], l[JC];
-    float4 o[JC];
+    float4 o[JC][DC];
 #pragma unroll
     for (int c = 0; c < JC; ++c) {
       const int j = j0 + c;
       l[c] = j < p.nq ? red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j] : 0.f;
       m[c] = l[c] > 0.f ? stash_m[j] : -INFINITY;
-      o[c] = l[c] > 0.f ? *reinterpret_cast<const float4*>(stash + j * D + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < DC; ++k)
+        o[c][k] = l[c] > 0.f ? *reinterpret_cast<const float4*>(stash + j * DIM + k * D + 4 * lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll 1
     for (int s = 0; s < nseg; ++s) {
       if (s == own) continue;
       float2 e[JC];
-      float4 v[JC];
+      float4 v[JC][DC];
 #pragma unroll
       for (int c = 0; c < JC; ++c) {
         const int j = j0 + c;
         if (j < p.nq) {
           const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
           e[c] = __ldcg(ml + part);
-          v[c] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * D) + lane);
+#pragma unroll
+          for (int k = 0; k < DC; ++k)
+            v[c][k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * DIM + k * D) + lane);
         } else {
           e[c] = make_float2(0.f, 0.f);
-          v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < DC; ++k) v[c][k] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
 #pragma unroll
@@ -290,8 +303,10 @@ OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int l
         if (e[c].y > 0.f) {
           const float mn = fmaxf(m[c], e[c].x);
           const float a = ex2(m[c] - mn), b = ex2(e[c].x - mn);
-          o[c] = make_float4(fmaf(o[c].x, a, v[c].x * b), fmaf(o[c].y, a, v[c].y * b), fmaf(o[c].z, a, v[c].z * b),
-                             fmaf(o[c].w, a, v[c].w * b));
+#pragma unroll
+          for (int k = 0; k < DC; ++k)
+            o[c][k] = make_float4(fmaf(o[c][k].x, a, v[c][k].x * b), fmaf(o[c][k].y, a, v[c][k].y * b),
+                                  fmaf(o[c][k].z, a, v[c][k].z * b), fmaf(o[c][k].w, a, v[c][k].w * b));
           l[c] = fmaf(l[c], a, e[c].y * b);
           m[c] = mn;
         }
@@ -302,33 +317,38 @@ OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int l
       const int j = j0 + c;
       if (j < p.nq) {
         const int64_t rowh = ((int64_t)g * p.nq + j) * p.heads + h;
-        store_out4(p.out + rowh * D + 4 * lane, o[c], l[c] > 0.f ? 1.f / l[c] : 0.f);
+#pragma unroll
+        for (int k = 0; k < DC; ++k)
+          store_out4(p.out + rowh * DIM + k * D + 4 * lane, o[c][k], l[c] > 0.f ? 1.f / l[c] : 0.f);
       }
     }
   }
 }
 
-// Running merge of segments for JC query columns (lane l holds dims 4l .. 4l+3): max (log2 units), sum, output.
-// The merge is the combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max); a segment that saw no key
-// (sum 0) takes no part, whatever its max.
-template <int JC>
+// Running merge of segments for JC query columns (lane l holds dims 4l .. 4l+3 of each 128-dim chunk): max (log2
+// units), sum, output. The merge is the combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max); a segment
+// that saw no key (sum 0) takes no part, whatever its max.
+template <int JC, int DC>
 struct SegAcc {
   float m[JC], l[JC];
-  float4 o[JC];
+  float4 o[JC][DC];
   OMNI_DEV void clear() {
 #pragma unroll
     for (int c = 0; c < JC; ++c) {
       m[c] = -INFINITY;
       l[c] = 0.f;
-      o[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < DC; ++k) o[c][k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  OMNI_DEV void add(int c, float em, float el, const float4& ev) {
+  OMNI_DEV void add(int c, float em, float el, const float4* ev) {
     if (el > 0.f) {
       const float mn = fmaxf(m[c], em);
       const float a = ex2(m[c] - mn), b = ex2(em - mn);
-      o[c] = make_float4(fmaf(o[c].x, a, ev.x * b), fmaf(o[c].y, a, ev.y * b), fmaf(o[c].z, a, ev.z * b),
-                         fmaf(o[c].w, a, ev.w * b));
+#pragma unroll
+      for (int k = 0; k < DC; ++k)
+        o[c][k] = make_float4(fmaf(o[c][k].x, a, ev[k].x * b), fmaf(o[c][k].y, a, ev[k].y * b),
+                              fmaf(o[c][k].z, a, ev[k].z * b), fmaf(o[c][k].w, a, ev[k].w * b));
       l[c] = fmaf(l[c], a, el * b);
       m[c] = mn;
     }
@@ -337,24 +357,28 @@ struct SegAcc {
 
 // Adds the segments of unit (g, h), queries j0 .. j0+JC-1, other than `own`, from the partial arrays (read through
 // L2: other CTAs wrote them). Segments go outermost so that the chunk's loads of one segment are all in flight.
-template <int JC>
-OMNI_DEV void add_other_segments(SegAcc<JC>& acc, const Params& p, int g, int h, int j0, int own, int nseg, int lane) {
+template <int JC, int DIM>
+OMNI_DEV void add_other_segments(SegAcc<JC, DIM / D>& acc, const Params& p, int g, int h, int j0, int own, int nseg,
+                                 int lane) {
+  constexpr int DC = DIM / D;
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
 #pragma unroll 1
   for (int s = 0; s < nseg; ++s) {
     if (s == own) continue;
     float2 e[JC];
-    float4 v[JC];
+    float4 v[JC][DC];
 #pragma unroll
     for (int c = 0; c < JC; ++c) {
       const int j = j0 + c;
       if (j < p.nq) {
         const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
         e[c] = __ldcg(ml + part);
-        v[c] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * D) + lane);
+#pragma unroll
+        for (int k = 0; k < DC; ++k) v[c][k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * DIM + k * D) + lane);
       } else {
         e[c] = make_float2(0.f, 0.f);
-        v[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < DC; ++k) v[c][k] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
@@ -363,42 +387,50 @@ OMNI_DEV void add_other_segments(SegAcc<JC>& acc, const Params& p, int g, int h,
 }
 
 // Adds this CTA's own segment (its stash) and writes the unit's output rows j0 .. j0+JC-1.
-template <int JC>
-OMNI_DEV void finish_unit(SegAcc<JC>& acc, const Params& p, int g, int h, int j0, int lane, const float* red_l,
+template <int JC, int DIM>
+OMNI_DEV void finish_unit(SegAcc<JC, DIM / D>& acc, const Params& p, int g, int h, int j0, int lane, const float* red_l,
                           const float* stash_m, const float* stash) {
+  constexpr int DC = DIM / D;
 #pragma unroll
   for (int c = 0; c < JC; ++c) {
     const int j = j0 + c;
     if (j < p.nq) {
       const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
-      acc.add(c, stash_m[j], l, *reinterpret_cast<const float4*>(stash + j * D + 4 * lane));
+      float4 own[DC];
+#pragma unroll
+      for (int k = 0; k < DC; ++k) own[k] = *reinterpret_cast<const float4*>(stash + j * DIM + k * D + 4 * lane);
+      acc.add(c, stash_m[j], l, own);
       const int64_t rowh = ((int64_t)g * p.nq + j) * p.heads + h;
-      store_out4(p.out + rowh * D + 4 * lane, acc.o[c], acc.l[c] > 0.f ? 1.f / acc.l[c] : 0.f);
+#pragma unroll
+      for (int k = 0; k < DC; ++k)
+        store_out4(p.out + rowh * DIM + k * D + 4 * lane, acc.o[c][k], acc.l[c] > 0.f ? 1.f / acc.l[c] : 0.f);
     }
   }
 }
 
-// S^T[buf] = K_tile (slot ks) . Q^T  (thread 0).
-OMNI_DEV void issue_scores(uint32_t tbase, int buf, const unsigned char* kslot, const unsigned char* qs) {
+// S^T[buf] (+)= K chunk (slot) . Q chunk^T (thread 0): the keys' 128-dim chunk `chunk` of the head; chunks after the
+// first accumulate.
+OMNI_DEV void issue_scores(uint32_t tbase, int buf, const unsigned char* kslot, const unsigned char* qs, int chunk) {
   const uint32_t kaddr = smem_addr(kslot);
   const uint32_t qaddr = smem_addr(qs);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint64_t a = smem_desc(kaddr + (kk >> 2) * BOX_BYTES + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-    const uint64_t b = smem_desc(qaddr + (kk >> 2) * (NQP * 128) + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-    mma_bf16_ss(tbase + buf * NQP, a, b, IDESC_S, kk > 0 ? 1u : 0u);
+    const uint64_t b =
+        smem_desc(qaddr + (2 * chunk + (kk >> 2)) * (NQP * 128) + (kk & 3) * 32, 16, 1024, kLayoutSw128);
+    mma_bf16_ss(tbase + buf * NQP, a, b, IDESC_S, (chunk > 0 || kk > 0) ? 1u : 0u);
   }
 }
 
-// O^T[buf] = V_tile^T (slot vs) . P^T[buf]  (thread 0).
-OMNI_DEV void issue_values(uint32_t tbase, int buf, const unsigned char* vslot, const unsigned char* pbuf) {
+// O^T chunk (TMEM column dcol) = V chunk^T (slot) . P^T[buf]  (thread 0).
+OMNI_DEV void issue_values(uint32_t tbase, uint32_t dcol, const unsigned char* vslot, const unsigned char* pbuf) {
   const uint32_t vaddr = smem_addr(vslot);
   const uint32_t paddr = smem_addr(pbuf);
 #pragma unroll
   for (int kk = 0; kk < BN / 16; ++kk) {
     const uint64_t a = smem_desc(vaddr + kk * 2048, BOX_BYTES, 1024, kLayoutSw128);
     const uint64_t b = smem_desc(paddr + kk * 256, 128, 2048, kLayoutNone);
-    mma_bf16_ss(tbase + 2 * NQP + buf * NQP, a, b, IDESC_O, kk > 0 ? 1u : 0u);
+    mma_bf16_ss(tbase + dcol, a, b, IDESC_O, kk > 0 ? 1u : 0u);
   }
 }
 
@@ -410,18 +442,25 @@ OMNI_DEV void issue_values(uint32_t tbase, int buf, const unsigned char* vslot, 
 //   MMA (warp 5)        s_full[b]   <- S^T(tile) done      o_full[b]   <- O^T(tile) done
 //   softmax (warps 0-3) s_free[b], p_full[b], o_free[b] (128 arrivals each)
 //   queries (TMA by the producer, two buffers by unit parity): q_fill[q] <- bytes, q_done[q] <- unit's last S^T
-template <int NQT, int SLOTS>
-__global__ void __launch_bounds__(THREADS, 1)
+// DIM: head_dim, 128 or 512. A key tile is DIM / 128 chunks of 128 dims, each a ring slot of 32 KB: S^T accumulates
+// over the K chunks, O^T has one accumulator per V chunk. With more than one chunk, warp 8 zeroes the V rows past a
+// unit's keys in each chunk of its last tile (vfix[c] <- zeroed) before the MMA reads them.
+template <int NQT, int SLOTS, int DIM>
+__global__ void __launch_bounds__(threads_for(DIM), 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap_half,
                    const __grid_constant__ CUtensorMap vmap_half, const Params pin) {
-  using L = Smem<SLOTS>;
+  using L = Smem<SLOTS, DIM>;
+  constexpr int DC = DIM / D;  // 128-dim chunks per head
+  constexpr int THREADS = threads_for(DIM);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[SLOTS], empty[SLOTS];
   __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_fill[2], q_done[2], drain;
   __shared__ __align__(8) uint64_t seg_ready, seg_free;  // the stash holds a finished unit / was written out
+  __shared__ __align__(8) uint64_t vfix[DC];   // head_dim 512: a last tile's V chunk c has its stale rows zeroed
+  __shared__ __align__(8) uint64_t vtail[DC];  // ... and its load was issued (so its slot's phase is the current one)
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ volatile int issued_k, issued_v, q_issued;  // K / V tiles and query tiles the producers issued
@@ -452,11 +491,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&drain, 1);
     mbar_init(&seg_ready, 128);
     mbar_init(&seg_free, 1);
+    for (int c = 0; c < DC; ++c) {
+      mbar_init(&vfix[c], 1);
+      mbar_init(&vtail[c], 1);
+    }
     mbar_fence_init();
     abort_flag = 0;
     issued_k = issued_v = q_issued = 0;
   }
-  if (warp == 0) tmem_alloc(&tmem_base, TMEM_COLS);
+  if (warp == 0) tmem_alloc(&tmem_base, tmem_cols(DIM));
   if (warp == 4 && lane == 0) {
     prefetch_tmap(&kmap);
     prefetch_tmap(&qmap);
@@ -566,31 +609,41 @@ __global__ void __launch_bounds__(THREADS, 1)
             abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&q_fill[qb], NQP * D * 2);
-          tma_load_3d(qs + qb * (NQP * D * 2), &qmap, 0, h, ti.g * p.nq, &q_fill[qb]);
-          tma_load_3d(qs + qb * (NQP * D * 2) + NQP * 128, &qmap, 64, h, ti.g * p.nq, &q_fill[qb]);
+          mbar_arrive_expect_tx(&q_fill[qb], NQP * DIM * 2);
+#pragma unroll
+          for (int bx = 0; bx < DIM / 64; ++bx)
+            tma_load_3d(qs + qb * (NQP * DIM * 2) + bx * (NQP * 128), &qmap, bx * 64, h, ti.g * p.nq, &q_fill[qb]);
           q_issued = ++unit;
           if (unit == 1) OMNI_TRACE_AT(4006);
         }
-        const int slot = (is_k ? 0 : HALF) + it % HALF, use = it / HALF;
-        if (use >= 1 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
-          abort_flag = 1;
-          break;
-        }
         // A unit's last tile with at most 64 keys left loads 64-row boxes: the rows past the keys are masked (K) or
-        // zeroed (V) by the softmax warps whatever they hold.
+        // zeroed (V: by the softmax warps for head_dim 128, by warp 8 otherwise) whatever they hold.
         const bool short_tail = (int64_t)tt * BN + 64 >= ti.need;
         const CUtensorMap* m = short_tail ? map_half : map;
-        mbar_arrive_expect_tx(&full[slot], short_tail ? SLOT_BYTES / 2 : SLOT_BYTES);
-        tma_load_4d(smem + slot * SLOT_BYTES, m, 0, tt * BN, h, ti.g, &full[slot]);
-        tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, m, 64, tt * BN, h, ti.g, &full[slot]);
-        if (is_k) {
-          issued_k = it + 1;
-          OMNI_TRACE_AT(it * 8);
-        } else {
-          issued_v = it + 1;
-          OMNI_TRACE_AT(it * 8 + 1);
+        bool stop = false;
+#pragma unroll 1
+        for (int c = 0; c < DC; ++c) {  // the tile's 128-dim chunks, one ring slot each
+          const int ci = it * DC + c;
+          const int slot = (is_k ? 0 : HALF) + ci % HALF, use = ci / HALF;
+          if (use >= 1 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
+            abort_flag = 1;
+            stop = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[slot], short_tail ? SLOT_BYTES / 2 : SLOT_BYTES);
+          tma_load_4d(smem + slot * SLOT_BYTES, m, c * D, tt * BN, h, ti.g, &full[slot]);
+          tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, m, c * D + 64, tt * BN, h, ti.g, &full[slot]);
+          if (is_k) {
+            issued_k = ci + 1;
+          } else {
+            issued_v = ci + 1;
+            // A last tile's V chunk: warp 8 may now wait for its load (the slot's current phase is this chunk's).
+            if (DC > 1 && (int64_t)tt * BN + BN > ti.need) mbar_arrive(&vtail[c]);
+          }
         }
+        if (stop) break;
+        if (is_k) OMNI_TRACE_AT(it * 8);
+        else OMNI_TRACE_AT(it * 8 + 1);
       }
     }
     __syncwarp();
@@ -599,35 +652,51 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       TileIter ti = first_tile;
       int unit = -1;
-      auto scores = [&](int t) -> bool {  // S^T(t) = K(t) Q^T
+      auto scores = [&](int t) -> bool {  // S^T(t) = K(t) Q^T, accumulated over the head's 128-dim chunks
         const int b = t & 1, u = t >> 1;
-        const int slot = t % HALF;
         if (u >= 1 && !mbar_wait(&s_free[b], (u - 1) & 1)) return false;
-        if (!mbar_wait(&full[slot], (t / HALF) & 1)) return false;
-        tc_fence_after();
-        OMNI_TRACE_AT(t * 8 + 2);
-        issue_scores(tbase, b, smem + slot * SLOT_BYTES, qs + (unit & 1) * (NQP * D * 2));
-        tc_commit(&s_full[b]);
-        tc_commit(&empty[slot]);
+#pragma unroll 1
+        for (int c = 0; c < DC; ++c) {
+          const int ci = t * DC + c;
+          const int slot = ci % HALF;
+          if (!mbar_wait(&full[slot], (ci / HALF) & 1)) return false;
+          tc_fence_after();
+          if (c == 0) OMNI_TRACE_AT(t * 8 + 2);
+          issue_scores(tbase, b, smem + slot * SLOT_BYTES, qs + (unit & 1) * (NQP * DIM * 2), c);
+          if (c == DC - 1) tc_commit(&s_full[b]);
+          tc_commit(&empty[slot]);
+        }
         return true;
       };
-      auto values = [&](int t) -> bool {  // O^T(t) = V(t)^T P^T(t)
+      // O^T(t) = V(t)^T P^T(t), one accumulator per 128-dim chunk. tail: the index of this tile among the CTA's last
+      // tiles of units (head_dim 512: its V chunks wait until warp 8 has zeroed their stale rows), or -1.
+      auto values = [&](int t, int tail) -> bool {
         const int b = t & 1, u = t >> 1;
-        const int slot = HALF + t % HALF;
         if (u >= 1 && !mbar_wait(&o_free[b], (u - 1) & 1)) return false;
         if (!mbar_wait(&p_full[b], u & 1)) return false;
-        if (!mbar_wait(&full[slot], (t / HALF) & 1)) return false;
-        tc_fence_after();
-        OMNI_TRACE_AT(t * 8 + 3);
-        issue_values(tbase, b, smem + slot * SLOT_BYTES, smem + L::P_OFF + b * (NQP * BN * 2));
-        tc_commit(&o_full[b]);
-        tc_commit(&empty[slot]);
+#pragma unroll 1
+        for (int c = 0; c < DC; ++c) {
+          const int ci = t * DC + c;
+          const int slot = HALF + ci % HALF;
+          if (DC > 1 && tail >= 0) {
+            if (!mbar_wait(&vfix[c], tail & 1)) return false;
+          } else if (!mbar_wait(&full[slot], (ci / HALF) & 1)) {
+            return false;
+          }
+          tc_fence_after();
+          if (c == 0) OMNI_TRACE_AT(t * 8 + 3);
+          issue_values(tbase, ocol(b, c, DC), smem + slot * SLOT_BYTES, smem + L::P_OFF + b * (NQP * BN * 2));
+          if (c == DC - 1) tc_commit(&o_full[b]);
+          tc_commit(&empty[slot]);
+        }
         return true;
       };
       // Tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1) runs -- also
       // across a unit boundary, where the softmax finishes the old unit one tile late.
       bool ok = true;
-      int pend = -1;  // tile whose O^T is still to issue
+      int pend = -1;       // tile whose O^T is still to issue
+      int pend_tail = -1;  // its index among the last tiles of units (head_dim 512), or -1
+      int tails = 0;
       for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
         if (ti.t == 0 || it == 0) {
           ++unit;
@@ -635,10 +704,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (ok) ok = scores(it);
         if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
-        if (ok && pend >= 0) ok = values(pend);
+        if (ok && pend >= 0) ok = values(pend, pend_tail);
         pend = it;
+        pend_tail = DC > 1 && (int64_t)ti.t * BN + BN > ti.need ? tails++ : -1;
       }
-      if (ok && pend >= 0 && !abort_flag) ok = values(pend);
+      if (ok && pend >= 0 && !abort_flag) ok = values(pend, pend_tail);
       if (!ok) abort_flag = 1;
     }
     __syncwarp();
@@ -652,7 +722,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* red_l = reinterpret_cast<float*>(smem + L::RED_L_OFF);
     float* stash_m = reinterpret_cast<float*>(smem + L::STASH_M_OFF);
     float* stash = reinterpret_cast<float*>(smem + L::STASH_OFF);
-    float m[NQT], lpart[NQT], acc[NQT], scl[NQT];
+    float m[NQT], lpart[NQT], acc[DC][NQT], scl[NQT];  // acc: thread = head dim (c * 128 + tid) of chunk c
     int lim[NQT];
     int g = 0, h = 0, need = 0, tiles = 1;
     int64_t unit_pos0 = 0;
@@ -679,7 +749,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           lim[j] = j < p.nq ? (int)(lj > need ? need : lj) : 0;
           m[j] = 0.f;  // a guess; the first tile lowers it if its scores are far below, or raises it
           lpart[j] = 0.f;
-          acc[j] = 0.f;
+#pragma unroll
+          for (int c = 0; c < DC; ++c) acc[c][j] = 0.f;
         }
       }
       const int key = tt * BN + tid;
@@ -719,7 +790,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float mnew = first ? (tmax == -INFINITY ? m[j] : tmax) : fmaxf(m[j], tmax);
           scl[j] = ex2(m[j] - mnew);
           m[j] = mnew;
-          acc[j] *= scl[j];
+#pragma unroll
+          for (int c = 0; c < DC; ++c) acc[c][j] *= scl[j];
           lpart[j] *= scl[j];
         }
         named_sync(1, 128);
@@ -748,8 +820,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         *reinterpret_cast<uint4*>(pb + 2048 + tid * 16) =
             NQT > 8 ? make_uint4(wv[4], wv[5], wv[6], wv[7]) : make_uint4(0u, 0u, 0u, 0u);
       }
-      // A tile that ends inside the unit's keys: zero the V rows past them (they may hold anything).
-      if (tt * BN + BN > need) {
+      // A tile that ends inside the unit's keys: zero the V rows past them (they may hold anything). With more than
+      // one chunk per tile, warp 8 does this.
+      if (DC == 1 && tt * BN + BN > need) {
         const int vslot = HALF + it % HALF;
         if (!mbar_wait(&full[vslot], (it / HALF) & 1)) abort_flag = 1;
         if (key >= need) {
@@ -772,19 +845,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (tid == 0) OMNI_TRACE_AT(it * 8 + 6);
         tc_fence_after();
         __syncwarp();
-        float o[NQP];
-        tmem_ld16(tbase + lane_off + 2 * NQP + (b ^ 1) * NQP, o);
+        float o[DC][NQP];
+#pragma unroll
+        for (int c = 0; c < DC; ++c) tmem_ld16(tbase + lane_off + ocol(b ^ 1, c, DC), o[c]);
         tc_fence_before();
         mbar_arrive(&o_free[b ^ 1]);
         if (stashed) {
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) stash[j * D + tid] += o[j];
+          for (int c = 0; c < DC; ++c)
+#pragma unroll
+            for (int j = 0; j < NQT; ++j) stash[j * DIM + c * D + tid] += o[c][j];
           mbar_arrive(&seg_ready);  // the write-out warp takes it from here
           ++segs;
           stashed = false;
         } else {
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) acc[j] = fmaf(scl[j], o[j], acc[j]);
+          for (int c = 0; c < DC; ++c)
+#pragma unroll
+            for (int j = 0; j < NQT; ++j) acc[c][j] = fmaf(scl[j], o[c][j], acc[c][j]);
         }
       }
       pending = true;
@@ -807,18 +885,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         nx.advance();
         if (!nx.done) {
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) stash[j * D + tid] = acc[j];
+          for (int c = 0; c < DC; ++c)
+#pragma unroll
+            for (int j = 0; j < NQT; ++j) stash[j * DIM + c * D + tid] = acc[c][j];
           stashed = true;
         } else {
           if (!mbar_wait(&o_full[b], par)) abort_flag = 1;
           tc_fence_after();
           __syncwarp();
-          float o[NQP];
-          tmem_ld16(tbase + lane_off + 2 * NQP + b * NQP, o);
+          float o[DC][NQP];
+#pragma unroll
+          for (int c = 0; c < DC; ++c) tmem_ld16(tbase + lane_off + ocol(b, c, DC), o[c]);
           tc_fence_before();
           mbar_arrive(&o_free[b]);
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) stash[j * D + tid] = acc[j] + o[j];
+          for (int c = 0; c < DC; ++c)
+#pragma unroll
+            for (int j = 0; j < NQT; ++j) stash[j * DIM + c * D + tid] = acc[c][j] + o[c][j];
           pending = false;
           mbar_arrive(&seg_ready);
           ++segs;
@@ -850,7 +933,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int nseg = (int)((pos0 + kTileCost * (ti.tiles - 1)) / per - seg0 + 1);
         const bool whole = nseg == 1;
         unsigned* ctr = merge_here && !whole ? p.counters + (int64_t)ti.g * p.heads + ti.h : nullptr;
-        SegAcc<JC> acc;
+        SegAcc<JC, DC> acc;
         acc.clear();
         bool last = false;  // this CTA merges the unit
         // Only the unit's first CTA watches: it works on the unit at the end of its range, the others at the start of
@@ -861,7 +944,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           while (!__shfl_sync(0xffffffffu, mbar_test_wait(&seg_ready, segs & 1), 0)) {
             if (__shfl_sync(0xffffffffu, abort_flag != 0 || global_ns() - t0 > kWaitLimitNs, 0)) break;
             if (__shfl_sync(0xffffffffu, ld_acquire_gpu(ctr), 0) == (unsigned)(nseg - 1)) {
-              add_other_segments<JC>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);
+              add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);
               last = true;
               break;
             }
@@ -877,15 +960,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!last) {
           for (int j = 0; j < p.nq && j < NQT; ++j) {
             const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
-            const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
             const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-            if (whole && p.out) {
-              store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
-            } else {
-              const int64_t part = rowh * p.st + seg;
-              *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
-              if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+            const int64_t part = rowh * p.st + seg;
+#pragma unroll
+            for (int c = 0; c < DC; ++c) {
+              const float4 a = *reinterpret_cast<const float4*>(stash + j * DIM + c * D + 4 * lane);
+              if (whole && p.out) store_out4(p.out + rowh * DIM + c * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
+              else *reinterpret_cast<float4*>(p.part_o + part * DIM + c * D + 4 * lane) = a;
             }
+            if (!(whole && p.out) && lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
           }
           if (ctr) {
             __threadfence();  // this lane's partial stores before the count
@@ -897,8 +980,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         if (last) {
-          if (counted) add_other_segments<JC>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);  // else merged while waiting
-          finish_unit<JC>(acc, p, ti.g, ti.h, 0, lane, red_l, stash_m, stash);
+          if (counted) add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);  // else merged while waiting
+          finish_unit<JC, DIM>(acc, p, ti.g, ti.h, 0, lane, red_l, stash_m, stash);
           if (lane == 0) *ctr = 0;  // zero again for the next call
         }
         __syncwarp();
@@ -931,15 +1014,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!last) {
           for (int j = 0; j < p.nq && j < NQT; ++j) {
             const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
-            const float4 a = *reinterpret_cast<const float4*>(stash + j * D + 4 * lane);
             const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-            if (whole && p.out) {
-              store_out4(p.out + rowh * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
-            } else {
-              const int64_t part = rowh * p.st + seg;
-              *reinterpret_cast<float4*>(p.part_o + part * D + 4 * lane) = a;
-              if (lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
+            const int64_t part = rowh * p.st + seg;
+#pragma unroll
+            for (int c = 0; c < DC; ++c) {
+              const float4 a = *reinterpret_cast<const float4*>(stash + j * DIM + c * D + 4 * lane);
+              if (whole && p.out) store_out4(p.out + rowh * DIM + c * D + 4 * lane, a, l > 0.f ? 1.f / l : 0.f);
+              else *reinterpret_cast<float4*>(p.part_o + part * DIM + c * D + 4 * lane) = a;
             }
+            if (!(whole && p.out) && lane == 0) reinterpret_cast<float2*>(p.part_ml)[part] = make_float2(stash_m[j], l);
           }
           if (ctr) {
             __threadfence();  // this lane's partial stores before the count
@@ -951,13 +1034,47 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (last) {
           __threadfence();  // the other CTAs' partials after their counts
-          merge_unit<NQT>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
+          merge_unit<NQT, DIM>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
           if (lane == 0) *ctr = 0;  // zero again for the next call
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&seg_free);
         ++segs;
       }
+    }
+  } else if (DC > 1 && warp == 8) {
+    // ------------------------------------------------------------------ head_dim 512: stale V rows of last tiles
+    // A unit's last tile may end inside the tile; the V rows past the unit's keys hold whatever the cache (or an
+    // earlier load into the slot) holds there, possibly NaN, and P^T is zero there but 0 x NaN is NaN. For each V
+    // chunk of such a tile: wait for its load, zero those rows (16-byte stores over the warp), make them visible to
+    // the tensor core and hand the chunk to the MMA issuer (vfix[c]: one phase per such tile).
+    // The chunk's load is awaited only after the V producer has issued it (vtail[c]): the warp walks its tiles
+    // without waiting on the others, and a parity wait on a slot whose current phase is two behind would pass at once.
+    int it = 0, tails = 0;
+    for (TileIter ti = first_tile; !ti.done && !abort_flag; ti.advance(), ++it) {
+      if ((int64_t)ti.t * BN + BN <= ti.need) continue;
+      const int valid = (int)(ti.need - (int64_t)ti.t * BN);  // rows 0 .. valid-1 hold keys
+      bool stop = false;
+#pragma unroll 1
+      for (int c = 0; c < DC; ++c) {
+        const int ci = it * DC + c;
+        const int slot = HALF + ci % HALF;
+        if (!mbar_wait_or(&vtail[c], tails & 1, &abort_flag) || !mbar_wait_or(&full[slot], (ci / HALF) & 1, &abort_flag)) {
+          abort_flag = 1;
+          stop = true;
+          break;
+        }
+        unsigned char* base = smem + slot * SLOT_BYTES;
+        for (int i = lane; i < (BN - valid) * 16; i += 32) {  // 16 16-byte words per row: 8 in each 64-column box
+          const int r = valid + (i >> 4), k = i & 15;
+          *reinterpret_cast<uint4*>(base + (k >> 3) * BOX_BYTES + r * 128 + (k & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&vfix[c]);
+      }
+      if (stop) break;
+      ++tails;
     }
   }
   __syncthreads();
@@ -981,7 +1098,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tbase, TMEM_COLS);
+    tmem_dealloc(tbase, tmem_cols(DIM));
   }
   if (tid == 0) OMNI_TRACE_AT(4021);
   OMNI_TRACE_CTA(1);
@@ -989,14 +1106,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // Merges the segments of each (query row, head): out = sum w_s o_s / sum w_s l_s. For beam search it first attends
 // the row's generated keys itself (they do not depend on the pass, so this overlaps the pass's tail): warp w scores 8
-// of each 32 keys (lane l holds dims 4l..4l+3; all 8 loads in flight, then butterfly sums), and thread d accumulates
-// dim d over the chunk's V rows; the result is one more segment. A unit the pass finished inside one CTA was written
-// by the pass itself.
+// of each 32 keys (lane l holds dims 4l..4l+3 of every 128-dim chunk; all 8 loads in flight, then butterfly sums), and
+// thread d accumulates dims d, d + 128, .. over the chunk's V rows; the result is one more segment. A unit the pass
+// finished inside one CTA was written by the pass itself.
+template <int DIM>
 __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int grid, __nv_bfloat16* __restrict__ out,
                                                          const GenKeys gen) {
+  constexpr int DC = DIM / D;
   __shared__ long long red_total[4], red_pre[4];
   __shared__ long long unit_tiles;
-  __shared__ float qs[D];
+  __shared__ float qs[DIM];
   __shared__ float sc[32];
   __shared__ long long koff[32];
   const int64_t rh = blockIdx.x;
@@ -1006,14 +1125,17 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
 
-  float gm = -INFINITY, gl = 0.f, go = 0.f;  // the generated keys' segment
+  float gm = -INFINITY, gl = 0.f, go[DC];  // the generated keys' segment
+#pragma unroll
+  for (int c = 0; c < DC; ++c) go[c] = 0.f;
   if (gen.enabled) {
-    qs[t] = __bfloat162float(p.q[rh * D + t]);
+#pragma unroll
+    for (int c = 0; c < DC; ++c) qs[c * D + t] = __bfloat162float(p.q[rh * DIM + c * D + t]);
     int64_t n = gen.gen_len[row];
     n = n < 0 ? 0 : (n > gen.cache_len ? gen.cache_len : n);
     __syncthreads();
     for (int64_t j0 = 0; j0 < n; j0 += 32) {
-      uint2 kv[8];
+      uint2 kv[8][DC];
       long long off[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -1028,14 +1150,19 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
           }
         }
         off[i] = src * gen.s_kb + (int64_t)h * gen.s_kh + j * gen.s_ks;
-        kv[i] = j < n ? *reinterpret_cast<const uint2*>(gen.k + off[i] + 4 * lane) : make_uint2(0u, 0u);
+#pragma unroll
+        for (int c = 0; c < DC; ++c)
+          kv[i][c] = j < n ? *reinterpret_cast<const uint2*>(gen.k + off[i] + c * D + 4 * lane) : make_uint2(0u, 0u);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float d = __uint_as_float(kv[i].x << 16) * qs[4 * lane] +
-                  __uint_as_float(kv[i].x & 0xffff0000u) * qs[4 * lane + 1] +
-                  __uint_as_float(kv[i].y << 16) * qs[4 * lane + 2] +
-                  __uint_as_float(kv[i].y & 0xffff0000u) * qs[4 * lane + 3];
+        float d = 0.f;
+#pragma unroll
+        for (int c = 0; c < DC; ++c) {
+          const float* qc = qs + c * D + 4 * lane;
+          d += __uint_as_float(kv[i][c].x << 16) * qc[0] + __uint_as_float(kv[i][c].x & 0xffff0000u) * qc[1] +
+               __uint_as_float(kv[i][c].y << 16) * qc[2] + __uint_as_float(kv[i][c].y & 0xffff0000u) * qc[3];
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
         if (lane == 0) {
@@ -1050,16 +1177,20 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
       for (int i = 0; i < 32; ++i) cm = fmaxf(cm, sc[i]);
       const float mnew = fmaxf(gm, cm);
       const float scale = ex2(gm - mnew);  // 0 for the first chunk
-      go *= scale;
+#pragma unroll
+      for (int c = 0; c < DC; ++c) go[c] *= scale;
       gl *= scale;
-      __nv_bfloat16 vv[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) vv[i] = j0 + i < n ? gen.v[koff[i] + t] : __float2bfloat16_rn(0.f);
+      for (int c = 0; c < DC; ++c) {
+        __nv_bfloat16 vv[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float pi = j0 + i < n ? ex2(sc[i] - mnew) : 0.f;
-        gl += pi;
-        go = fmaf(pi, __bfloat162float(vv[i]), go);
+        for (int i = 0; i < 32; ++i) vv[i] = j0 + i < n ? gen.v[koff[i] + c * D + t] : __float2bfloat16_rn(0.f);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float pi = j0 + i < n ? ex2(sc[i] - mnew) : 0.f;
+          if (c == 0) gl += pi;
+          go[c] = fmaf(pi, __bfloat162float(vv[i]), go[c]);
+        }
       }
       gm = mnew;
       __syncthreads();  // sc / koff are refilled by the next chunk
@@ -1103,23 +1234,28 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   float mx = gl > 0.f ? gm : -INFINITY;
   for (int s = 0; s < nseg; ++s)
     if (ml[s].y > 0.f) mx = fmaxf(mx, ml[s].x);
-  float o = 0.f, l = 0.f;
+  float o[DC], l = 0.f;
+#pragma unroll
+  for (int c = 0; c < DC; ++c) o[c] = 0.f;
   if (mx != -INFINITY) {
     for (int s = 0; s < nseg; ++s) {
       const float2 e = ml[s];
       if (e.y > 0.f) {
         const float wgt = ex2(e.x - mx);
-        o = fmaf(wgt, p.part_o[(rh * p.st + s) * D + t], o);
+#pragma unroll
+        for (int c = 0; c < DC; ++c) o[c] = fmaf(wgt, p.part_o[(rh * p.st + s) * DIM + c * D + t], o[c]);
         l = fmaf(wgt, e.y, l);
       }
     }
     if (gl > 0.f) {
       const float wgt = ex2(gm - mx);
-      o = fmaf(wgt, go, o);
+#pragma unroll
+      for (int c = 0; c < DC; ++c) o[c] = fmaf(wgt, go[c], o[c]);
       l = fmaf(wgt, gl, l);
     }
   }
-  out[rh * D + t] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+#pragma unroll
+  for (int c = 0; c < DC; ++c) out[rh * DIM + c * D + t] = __float2bfloat16_rn(l > 0.f ? o[c] / l : 0.f);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1135,10 +1271,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_cache_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int64_t len, int64_t s_row,
-                    int64_t s_head, int64_t s_pos, int box_rows = BN) {
+                    int64_t s_head, int64_t s_pos, int dim, int box_rows = BN) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t dims[4] = {(cuuint64_t)dim, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)rows};
   cuuint64_t strides[3] = {(cuuint64_t)s_pos * 2, (cuuint64_t)s_head * 2, (cuuint64_t)s_row * 2};
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -1148,12 +1284,12 @@ bool make_cache_map(CUtensorMap* map, const void* base, int64_t rows, int heads,
   return r == CUDA_SUCCESS;
 }
 
-// Queries [rows, heads, 128] as 16-row boxes of one head (two 64-column boxes per unit), 128-byte swizzle.
-bool make_query_map(CUtensorMap* map, const void* q, int64_t rows, int heads) {
+// Queries [rows, heads, dim] as 16-row boxes of one head (dim / 64 boxes of 64 columns per unit), 128-byte swizzle.
+bool make_query_map(CUtensorMap* map, const void* q, int64_t rows, int heads, int dim) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)rows};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
+  cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)dim * 2, (cuuint64_t)heads * dim * 2};
   cuuint32_t box[3] = {64, 1, (cuuint32_t)NQP};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
@@ -1169,7 +1305,7 @@ bool tc_path_enabled(int dtype, int dim, int nq) {
     const char* e = getenv("OMNIASR_ATTN_PATH");
     return e && e[0] == 'c';  // "cuda_cores"
   }();
-  return !forced_off && dtype == kBF16 && dim == tcattn::D && nq >= 1 && nq <= tcattn::NQP &&
+  return !forced_off && dtype == kBF16 && (dim == 128 || dim == 512) && nq >= 1 && nq <= tcattn::NQP &&
          tcattn::encode_fn() != nullptr;
 }
 
@@ -1202,13 +1338,14 @@ int tc_unit_cost(int nq) {
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream) {
   using namespace tcattn;
+  if (p.dim != 128 && p.dim != 512) return cudaErrorInvalidValue;
   CUtensorMap kmap, vmap, kmap_half, vmap_half;
   CUtensorMap qmap;
-  if (!make_cache_map(&kmap, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
-      !make_cache_map(&vmap, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos) ||
-      !make_cache_map(&kmap_half, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, 64) ||
-      !make_cache_map(&vmap_half, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, 64) ||
-      !make_query_map(&qmap, p.q, (int64_t)p.groups * p.nq, p.heads))
+  if (!make_cache_map(&kmap, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, p.dim) ||
+      !make_cache_map(&vmap, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, p.dim) ||
+      !make_cache_map(&kmap_half, k, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, p.dim, 64) ||
+      !make_cache_map(&vmap_half, v, cache_rows, p.heads, cache_len, s_row, s_head, s_pos, p.dim, 64) ||
+      !make_query_map(&qmap, p.q, (int64_t)p.groups * p.nq, p.heads, p.dim))
     return cudaErrorInvalidValue;
   p.cap = cache_len < keys ? cache_len : keys;
   p.st = tc_segments(keys);
@@ -1216,21 +1353,27 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   p.unit_cost = tc_unit_cost(p.nq);
   p.prefetch = tc_prefetch();
   using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
-  static const Kern table[5] = {attn_tc_kernel<1, 6>, attn_tc_kernel<2, 6>, attn_tc_kernel<4, 6>,
-                                attn_tc_kernel<8, 6>, attn_tc_kernel<16, 6>};
+  // head_dim 128: six 32 KB ring slots (three K and three V tiles in flight); head_dim 512: four (two chunks each),
+  // as the query buffers and the stash grow four-fold.
+  static const Kern table[2][5] = {
+      {attn_tc_kernel<1, 6, 128>, attn_tc_kernel<2, 6, 128>, attn_tc_kernel<4, 6, 128>, attn_tc_kernel<8, 6, 128>,
+       attn_tc_kernel<16, 6, 128>},
+      {attn_tc_kernel<1, 4, 512>, attn_tc_kernel<2, 4, 512>, attn_tc_kernel<4, 4, 512>, attn_tc_kernel<8, 4, 512>,
+       attn_tc_kernel<16, 4, 512>}};
+  const int di = p.dim == 128 ? 0 : 1;
   const int ci = p.nq <= 1 ? 0 : p.nq <= 2 ? 1 : p.nq <= 4 ? 2 : p.nq <= 8 ? 3 : 4;
-  const Kern kern = table[ci];
-  const int bytes = Smem<6>::BYTES;
-  static bool configured[5] = {};
-  if (!configured[ci]) {
+  const Kern kern = table[di][ci];
+  const int bytes = di == 0 ? Smem<6, 128>::BYTES : Smem<4, 512>::BYTES;
+  static bool configured[2][5] = {};
+  if (!configured[di][ci]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
-    configured[ci] = true;
+    configured[di][ci] = true;
   }
   // Programmatic dependent launch: the set-up above griddepcontrol.wait overlaps the previous kernel.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(threads_for(p.dim));
   cfg.dynamicSmemBytes = (size_t)bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1256,10 +1399,11 @@ cudaError_t launch_tc_combine(const TcParams& p, void* out, const GenKeys& gen, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_tc_kernel, p, p.grid, o, gen);
+  auto kern = p.dim == 512 ? combine_tc_kernel<512> : combine_tc_kernel<128>;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, p.grid, o, gen);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();  // no programmatic launch here: an ordinary one
-    combine_tc_kernel<<<cfg.gridDim, cfg.blockDim, 0, stream>>>(p, p.grid, o, gen);
+    kern<<<cfg.gridDim, cfg.blockDim, 0, stream>>>(p, p.grid, o, gen);
     e = cudaGetLastError();
   }
   return e;

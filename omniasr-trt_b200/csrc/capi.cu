@@ -219,6 +219,7 @@ static int group_attention(const char* name, const void* q, const void* k_cache,
     t.nq = nq;
     t.causal = causal;
     t.heads = heads;
+    t.dim = dim;
     t.qscale = scale * omni::kLog2e;
     t.status = status;
     t.out = static_cast<__nv_bfloat16*>(out);
@@ -351,6 +352,7 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
     t.nq = beams;
     t.causal = 0;
     t.heads = heads;
+    t.dim = dim;
     t.qscale = scale * omni::kLog2e;
     t.status = status;
     omni::carve_partials(workspace, rows, heads, stc, dim, &t.part_o, &t.part_ml);
