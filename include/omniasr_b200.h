@@ -130,6 +130,21 @@ int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_str
                               int batch, int heads, int width, int dim, float scale, int dtype, int* status,
                               cudaStream_t stream);
 
+/* Causal prefill attention on the tensor-core decode pass, for head_dims without a dedicated prefill kernel (the
+ * shipped model's 512; 128 also works): each batch row's `width` query positions are cut into groups of 16
+ * consecutive positions, group j attending, as a 16-token draft, to keys [0, 16j + 1 + i) of the row's cache.
+ * q and out are [batch * wp, heads, dim] contiguous with wp = width rounded up to a multiple of 16 (row b's query w
+ * at row b * wp + w; the padding rows are computed and may be ignored); k_cache / v_cache are [>= batch, heads,
+ * >= width, dim] views as for omniasr_draft_attention. batch * (wp / 16) * heads <= 16384 per call. The workspace
+ * (omniasr_prefill_grouped_workspace() bytes) starts with unit counters that must be zero on entry; every call leaves
+ * them zero. Replaces, like omniasr_prefill_attention, the prefill's F.scaled_dot_product_attention(q, k, v,
+ * is_causal=True) of omniasr_trt/decode.py:171. */
+size_t omniasr_prefill_grouped_workspace(int batch, int heads, int width, int dim);
+int omniasr_prefill_attention_grouped(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                                      int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                                      void* out, int batch, int heads, int width, int dim, float scale, int dtype,
+                                      void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
+
 /* Beam reorder: dst row r (r < rows <= 65535) = src row parent[r], byte-exact; rows are row_bytes long,
  * strides in bytes; parent is int32 (parent_is_int64 = 0) or int64. src and dst must not overlap.
  * Replaces the K/V `index_select(0, parent)` of omniasr_trt/llm.py:237-238 and the pointer /

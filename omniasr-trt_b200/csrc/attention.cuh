@@ -64,6 +64,8 @@ struct TcParams {
   const int64_t* lengths;  // [groups]
   int groups, nq, causal, heads;
   int dim;        // head_dim: 128 or 512
+  int kv_div;     // groups per cache row: group g reads cache row g / kv_div (1 but in prefill mode)
+  int prefill;    // prefill mode: lengths[g] = (g % kv_div) * nq + 1, partials indexed by the unit's first CTA
   int64_t cap;    // min(cache length, keys): keys a unit may read (set by launch_tc_pass)
   float qscale;   // softmax scale * log2(e)
   float* part_o;  // [groups * nq, heads, st, dim]
@@ -86,6 +88,12 @@ constexpr size_t kCounterBytes = kCounterUnits * sizeof(unsigned);
 
 bool tc_path_enabled(int dtype, int dim, int nq);
 int tc_segments(int64_t keys);
+int tc_grid();
+int tc_unit_cost(int nq);
+// Prefill mode of the pass: the segments a unit can span (the partial slots per CTA) for batch rows of `width`
+// queries in groups of `nq`, and the workspace bytes (unit counters, then the compact partials).
+int tc_prefill_segments(int batch, int heads, int width, int nq);
+size_t tc_prefill_workspace(int batch, int heads, int width, int dim, int nq);
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream);
 // Beam search's generated keys, attended inside the combine (before it waits for the pass): row r's key j < gen_len[r]

@@ -23,6 +23,8 @@
 // (kernels.py:146-161 / :197-211).
 
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 #include <math.h>
 #include <stdlib.h>
 
@@ -65,9 +67,21 @@ constexpr uint32_t IDESC_O = idesc_bf16(128, NQP, 1, 1);
 
 using Params = TcParams;
 
+// Group g's length: lengths[g], or in prefill mode (a row's queries as groups of nq consecutive positions, kv_div
+// groups per cache row) the keys its first query sees, (g % kv_div) * nq + 1.
+OMNI_DEV int64_t group_len(const Params& p, int g) {
+  return p.prefill ? (int64_t)(g % p.kv_div) * p.nq + 1 : p.lengths[g];
+}
+
+// Index of segment s of query row j of unit (g, h) in the partial arrays. In prefill mode only the units cut between
+// CTAs have partials, and each CTA is the first CTA of at most one of them: the slot is that CTA's (seg0).
+OMNI_DEV int64_t part_index(const Params& p, int g, int j, int h, int s, int64_t seg0) {
+  return p.prefill ? (seg0 * p.st + s) * NQP + j : (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
+}
+
 // Keys unit (g, .) must read, clamped to the cache and the key bound.
 OMNI_DEV int64_t unit_need(const Params& p, int g) {
-  int64_t n = p.lengths[g] + (p.causal ? p.nq - 1 : 0);
+  int64_t n = group_len(p, g) + (p.causal ? p.nq - 1 : 0);
   n = n < 0 ? 0 : n;
   return n > p.cap ? p.cap : n;
 }
@@ -259,7 +273,7 @@ OMNI_DEV void store_out4(__nv_bfloat16* dst, const float4& a, float inv) {
 // once; the merge is the combine's: out = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max), segments that saw no
 // key take no part.
 template <int NQT, int DIM>
-OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int lane, const float* red_l,
+OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int64_t seg0, int lane, const float* red_l,
                          const float* stash_m, const float* stash) {
   constexpr int DC = DIM / D;
   constexpr int JC = (NQT < 8 ? NQT : 8) / DC > 0 ? (NQT < 8 ? NQT : 8) / DC : 1;  // queries per chunk (registers)
@@ -287,7 +301,7 @@ OMNI_DEV void merge_unit(const Params& p, int g, int h, int own, int nseg, int l
       for (int c = 0; c < JC; ++c) {
         const int j = j0 + c;
         if (j < p.nq) {
-          const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
+          const int64_t part = part_index(p, g, j, h, s, seg0);
           e[c] = __ldcg(ml + part);
 #pragma unroll
           for (int k = 0; k < DC; ++k)
@@ -359,7 +373,7 @@ struct SegAcc {
 // L2: other CTAs wrote them). Segments go outermost so that the chunk's loads of one segment are all in flight.
 template <int JC, int DIM>
 OMNI_DEV void add_other_segments(SegAcc<JC, DIM / D>& acc, const Params& p, int g, int h, int j0, int own, int nseg,
-                                 int lane) {
+                                 int64_t seg0, int lane) {
   constexpr int DC = DIM / D;
   const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
 #pragma unroll 1
@@ -371,7 +385,7 @@ OMNI_DEV void add_other_segments(SegAcc<JC, DIM / D>& acc, const Params& p, int 
     for (int c = 0; c < JC; ++c) {
       const int j = j0 + c;
       if (j < p.nq) {
-        const int64_t part = (((int64_t)g * p.nq + j) * p.heads + h) * p.st + s;
+        const int64_t part = part_index(p, g, j, h, s, seg0);
         e[c] = __ldcg(ml + part);
 #pragma unroll
         for (int k = 0; k < DC; ++k) v[c][k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + part * DIM + k * D) + lane);
@@ -523,7 +537,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
   if (p.groups <= kSmemGroups) {
     int64_t c = 0;
     if (tid < p.groups) {
-      const int64_t len = pin.lengths[tid];
+      const int64_t len = group_len(pin, tid);
       s_len[tid] = len;
       int64_t n = len + (p.causal ? p.nq - 1 : 0);
       n = n < 0 ? 0 : (n > p.cap ? p.cap : n);
@@ -549,7 +563,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
     // What the combine would otherwise do for the units without a segment: report lengths outside the cache and
     // give the rows that see no key zeros (their units have no tiles, so no CTA of the pass visits them).
     if (blockIdx.x == 0) {
-      for (int g = tid; g < p.groups; g += THREADS) {
+      for (int g = tid; g < p.groups && !p.prefill; g += THREADS) {  // prefill mode clamps its padding rows
         const int64_t raw = p.lengths[g] + (p.causal ? p.nq - 1 : 0);
         if (p.lengths[g] < 0 || raw > p.cap) raise_status(p.status, kStatusIndex);
       }
@@ -631,8 +645,9 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
             break;
           }
           mbar_arrive_expect_tx(&full[slot], short_tail ? SLOT_BYTES / 2 : SLOT_BYTES);
-          tma_load_4d(smem + slot * SLOT_BYTES, m, c * D, tt * BN, h, ti.g, &full[slot]);
-          tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, m, c * D + 64, tt * BN, h, ti.g, &full[slot]);
+          const int crow = ti.g / p.kv_div;  // the group's cache row
+          tma_load_4d(smem + slot * SLOT_BYTES, m, c * D, tt * BN, h, crow, &full[slot]);
+          tma_load_4d(smem + slot * SLOT_BYTES + BOX_BYTES, m, c * D + 64, tt * BN, h, crow, &full[slot]);
           if (is_k) {
             issued_k = ci + 1;
           } else {
@@ -741,7 +756,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
         tiles = (int)ti.tiles;
         need = (int)ti.need;
         unit_pos0 = ti.unit_pos0();
-        const int64_t n = p.lengths[g];
+        const int64_t n = group_len(p, g);
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
           int64_t lj = n + (p.causal ? j : 0);
@@ -944,7 +959,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
           while (!__shfl_sync(0xffffffffu, mbar_test_wait(&seg_ready, segs & 1), 0)) {
             if (__shfl_sync(0xffffffffu, abort_flag != 0 || global_ns() - t0 > kWaitLimitNs, 0)) break;
             if (__shfl_sync(0xffffffffu, ld_acquire_gpu(ctr), 0) == (unsigned)(nseg - 1)) {
-              add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);
+              add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, seg0, lane);
               last = true;
               break;
             }
@@ -961,7 +976,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
           for (int j = 0; j < p.nq && j < NQT; ++j) {
             const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
             const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-            const int64_t part = rowh * p.st + seg;
+            const int64_t part = part_index(p, ti.g, j, ti.h, seg, seg0);
 #pragma unroll
             for (int c = 0; c < DC; ++c) {
               const float4 a = *reinterpret_cast<const float4*>(stash + j * DIM + c * D + 4 * lane);
@@ -980,7 +995,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
           }
         }
         if (last) {
-          if (counted) add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, lane);  // else merged while waiting
+          if (counted) add_other_segments<JC, DIM>(acc, p, ti.g, ti.h, 0, seg, nseg, seg0, lane);  // else merged
           finish_unit<JC, DIM>(acc, p, ti.g, ti.h, 0, lane, red_l, stash_m, stash);
           if (lane == 0) *ctr = 0;  // zero again for the next call
         }
@@ -1015,7 +1030,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
           for (int j = 0; j < p.nq && j < NQT; ++j) {
             const float l = red_l[j] + red_l[NQP + j] + red_l[2 * NQP + j] + red_l[3 * NQP + j];
             const int64_t rowh = ((int64_t)ti.g * p.nq + j) * p.heads + ti.h;
-            const int64_t part = rowh * p.st + seg;
+            const int64_t part = part_index(p, ti.g, j, ti.h, seg, seg0);
 #pragma unroll
             for (int c = 0; c < DC; ++c) {
               const float4 a = *reinterpret_cast<const float4*>(stash + j * DIM + c * D + 4 * lane);
@@ -1034,7 +1049,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
         }
         if (last) {
           __threadfence();  // the other CTAs' partials after their counts
-          merge_unit<NQT, DIM>(p, ti.g, ti.h, seg, nseg, lane, red_l, stash_m, stash);
+          merge_unit<NQT, DIM>(p, ti.g, ti.h, seg, nseg, seg0, lane, red_l, stash_m, stash);
           if (lane == 0) *ctr = 0;  // zero again for the next call
         }
         __syncwarp();
@@ -1219,7 +1234,7 @@ __global__ void __launch_bounds__(128) combine_tc_kernel(const Params p, int gri
   const long long tiles = unit_tiles;
   const long long pos0 =
       red_pre[0] + red_pre[1] + red_pre[2] + red_pre[3] + (long long)h * unit_cost(p, tiles) + p.unit_cost;
-  if (t == 0 && h == 0 && row % p.nq == 0) {
+  if (t == 0 && h == 0 && row % p.nq == 0 && !p.prefill) {
     const int64_t raw = p.lengths[g] + (p.causal ? p.nq - 1 : 0);
     if (p.lengths[g] < 0 || raw > p.cap) raise_status(p.status, kStatusIndex);
   }
@@ -1335,6 +1350,44 @@ int tc_unit_cost(int nq) {
   return nq <= 1 ? 0 : 10;
 }
 
+int tc_prefill_segments(int batch, int heads, int width, int nq) {
+  // The pass's own schedule (TileIter): unit (g, h) costs unit_cost + kTileCost * tiles at cost position pre(g) +
+  // h * ucost(g); CTA b owns [b * per, (b + 1) * per). Group g = row * gpr + j covers queries 16j .. 16j + 15 and
+  // reads min(16j + nq, width) keys.
+  using namespace tcattn;
+  const int gpr = (width + nq - 1) / nq;
+  const int64_t ucost = tc_unit_cost(nq);
+  auto cost = [&](int j) -> int64_t {
+    const int64_t need = std::min<int64_t>((int64_t)j * nq + nq, width);
+    const int64_t tiles = (need + BN - 1) / BN;
+    return tiles > 0 ? ucost + kTileCost * tiles : 0;
+  };
+  int64_t total = 0;
+  for (int j = 0; j < gpr; ++j) total += cost(j) * heads;
+  total *= batch;
+  const int grid = tc_grid();
+  const int64_t per = std::max<int64_t>((total + grid - 1) / grid, kTileCost);
+  int most = 1;
+  int64_t pre = 0;
+  for (int b = 0; b < batch; ++b)
+    for (int j = 0; j < gpr; ++j) {
+      const int64_t c = cost(j);
+      const int64_t tiles = (c - ucost) / kTileCost;
+      for (int h = 0; h < heads && tiles > 0; ++h) {
+        const int64_t pos0 = pre + h * c + ucost;
+        const int nseg = (int)((pos0 + kTileCost * (tiles - 1)) / per - pos0 / per + 1);
+        most = std::max(most, nseg);
+      }
+      pre += c * heads;
+    }
+  return most;
+}
+
+size_t tc_prefill_workspace(int batch, int heads, int width, int dim, int nq) {
+  const int st = tc_prefill_segments(batch, heads, width, nq);
+  return kCounterBytes + partial_bytes((int64_t)tc_grid() * tcattn::NQP, 1, st, dim);
+}
+
 cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int64_t cache_len, int64_t s_row,
                            int64_t s_head, int64_t s_pos, int keys, TcParams& p, cudaStream_t stream) {
   using namespace tcattn;
@@ -1348,7 +1401,8 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
       !make_query_map(&qmap, p.q, (int64_t)p.groups * p.nq, p.heads, p.dim))
     return cudaErrorInvalidValue;
   p.cap = cache_len < keys ? cache_len : keys;
-  p.st = tc_segments(keys);
+  if (!p.prefill) p.st = tc_segments(keys);  // prefill mode: set by the caller (tc_prefill_segments)
+  if (p.kv_div < 1) p.kv_div = 1;
   p.grid = tc_grid();
   p.unit_cost = tc_unit_cost(p.nq);
   p.prefetch = tc_prefetch();

@@ -16,6 +16,9 @@
 
 static_assert(omni::kCounterBytes == OMNIASR_ATTENTION_COUNTER_BYTES, "counter prefix of the decode / draft workspace");
 
+// Query positions per group of the grouped prefill: the tensor-core pass's widest unit.
+constexpr int kPrefillGroup = 16;
+
 namespace {
 
 thread_local std::string g_error;
@@ -458,6 +461,61 @@ int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_str
   a.scale = scale;
   a.status = status;
   return cuda_status(omni::launch_prefill(a, stream), "prefill launch");
+}
+
+size_t omniasr_prefill_grouped_workspace(int batch, int heads, int width, int dim) {
+  if (batch <= 0 || heads <= 0 || width <= 0 || (dim != 128 && dim != 512)) return 0;
+  return omni::tc_prefill_workspace(batch, heads, width, dim, kPrefillGroup);
+}
+
+int omniasr_prefill_attention_grouped(const void* q, const void* k_cache, const void* v_cache, int64_t cache_rows,
+                                      int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos,
+                                      void* out, int batch, int heads, int width, int dim, float scale, int dtype,
+                                      void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+  const char* name = "prefill_attention_grouped";
+  if (dtype != OMNIASR_BF16 || (dim != 128 && dim != 512))
+    return fail(OMNIASR_ERR_UNSUPPORTED, "%s: bf16 with head_dim 128 or 512 (dtype %d, head_dim %d)", name, dtype,
+                dim);
+  if (int e = check_common(dtype, dim, heads)) return e;
+  if (batch < 0 || width < 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: batch %d width %d", name, batch, width);
+  if (batch == 0 || width == 0) return ok();
+  if (!q || !out) return fail(OMNIASR_ERR_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(q) || !aligned16(out)) return fail(OMNIASR_ERR_ARGUMENT, "%s: q / out not 16-byte aligned", name);
+  if (int e = check_cache(name, k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head, stride_pos, heads,
+                          dim, dtype))
+    return e;
+  if (batch > cache_rows || width > cache_len)
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: %d rows of width %d, cache [%lld rows, %lld positions]", name, batch,
+                width, (long long)cache_rows, (long long)cache_len);
+  const int gpr = (width + kPrefillGroup - 1) / kPrefillGroup;
+  const int64_t groups = (int64_t)batch * gpr;
+  if (groups * heads > omni::kCounterUnits)
+    return fail(OMNIASR_ERR_ARGUMENT, "%s: %lld query groups x %d heads exceed %d units per call (split the batch)",
+                name, (long long)groups, heads, omni::kCounterUnits);
+  const size_t need = omniasr_prefill_grouped_workspace(batch, heads, width, dim);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(OMNIASR_ERR_WORKSPACE, "%s: workspace %zu bytes, %zu needed (16-byte aligned)", name,
+                workspace ? workspace_bytes : (size_t)0, need);
+  omni::TcParams t{};
+  t.q = static_cast<const __nv_bfloat16*>(q);
+  t.lengths = nullptr;
+  t.groups = (int)groups;
+  t.nq = kPrefillGroup;
+  t.causal = 1;
+  t.heads = heads;
+  t.dim = dim;
+  t.kv_div = gpr;
+  t.prefill = 1;
+  t.st = omni::tc_prefill_segments(batch, heads, width, kPrefillGroup);
+  t.qscale = scale * omni::kLog2e;
+  t.status = status;
+  t.out = static_cast<__nv_bfloat16*>(out);
+  t.counters = static_cast<unsigned*>(workspace);
+  omni::carve_partials(static_cast<char*>(workspace) + omni::kCounterBytes, (int64_t)omni::tc_grid() * 16, 1, t.st,
+                       dim, &t.part_o, &t.part_ml);
+  return cuda_status(omni::launch_tc_pass(k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                                          stride_pos, width, t, stream),
+                     "grouped prefill launch");
 }
 
 int omniasr_reorder_gather(const void* src, int64_t src_row_stride, int64_t src_rows, void* dst,

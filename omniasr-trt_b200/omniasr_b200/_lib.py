@@ -39,6 +39,9 @@ SIGNATURES = {
                                     _i64, _p, _i64, _p, _p, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
     "omniasr_prefill_attention": (_i, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64,
                                        _i64, _i64, _i, _i, _i, _i, _f, _i, _p, _p]),
+    "omniasr_prefill_grouped_workspace": (_sz, [_i, _i, _i, _i]),
+    "omniasr_prefill_attention_grouped": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _i, _i, _i, _f, _i,
+                                               _p, _sz, _p, _p]),
     "omniasr_reorder_gather": (_i, [_p, _i64, _i64, _p, _i64, _p, _i, _i, _i64, _p, _p]),
     "omniasr_decode_attention_noalloc": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _i, _i, _f,
                                               _i, _p, _p]),

@@ -244,7 +244,8 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
     v typically cache views); query w sees keys [0, w]. Returns [B, H, W, D] in q's dtype -- a view of a
     [B, W, H, D] buffer, so the caller's ``o.transpose(1, 2).reshape(B * W, -1)`` costs nothing. This is the
     reference's ``F.scaled_dot_product_attention(q, k, v, is_causal=True)`` (decode.py:171): bf16 head_dim 128 runs
-    on the tensor cores; other dtypes / head dims run as a drafted verify with W queries per row."""
+    on the tensor-core prefill kernel, bf16 head_dim 512 on the tensor-core decode pass in groups of 16 query
+    positions; other dtypes / head dims run as a drafted verify with W queries per row on the CUDA cores."""
     b, heads, width, dim = q.shape
     scale = dim**-0.5 if scale is None else float(scale)
     out = torch.empty(b, width, heads, dim, dtype=q.dtype, device=q.device)
@@ -252,6 +253,8 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
         return out.transpose(1, 2)
     if k.shape != q.shape or v.shape != q.shape or q.stride(3) != 1 or k.stride(3) != 1 or v.stride(3) != 1:
         raise ValueError("prefill_attention: q, k, v must be [B, H, W, D] with unit stride in D")
+    if q.dtype == torch.bfloat16 and dim == 512:
+        return _prefill_grouped(q, k, v, scale)
     if q.dtype == torch.bfloat16 and dim == 128:
         _lib.call("omniasr_prefill_attention", _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k), k.stride(0),
                   k.stride(1), k.stride(2), _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(out), out.stride(0),
@@ -265,6 +268,33 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
     ones = torch.ones(b, dtype=torch.int64, device=q.device)
     o = draft_attention(qq, k, v, ones, width, width, scale)
     return o.view(b, width, heads, dim).transpose(1, 2)
+
+
+_PREFILL_GROUP = 16  # query positions per group of the grouped prefill
+
+
+def _prefill_grouped(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """bf16 head_dim 512: every row's queries as groups of 16 consecutive positions on the tensor-core decode pass
+    (omniasr_prefill_attention_grouped), the queries padded to a multiple of 16 positions; rows are split into calls
+    of at most 16384 (group, head) units."""
+    b, heads, width, dim = q.shape
+    wp = -(-width // _PREFILL_GROUP) * _PREFILL_GROUP
+    if k.stride() != v.stride() or k.stride(3) != 1:
+        k, v = k.contiguous(), v.contiguous()
+    qp = torch.zeros(b, wp, heads, dim, dtype=q.dtype, device=q.device)
+    qp[:, :width] = q.transpose(1, 2)
+    outp = torch.empty_like(qp)
+    rows_per_call = max(1, 16384 // ((wp // _PREFILL_GROUP) * heads))
+    lib = _lib.load()
+    for r0 in range(0, b, rows_per_call):
+        rb = min(rows_per_call, b - r0)
+        nbytes = lib.omniasr_prefill_grouped_workspace(rb, heads, width, dim)
+        ws = _attn_workspace(nbytes, q.device)
+        kk, vv = k[r0:r0 + rb], v[r0:r0 + rb]
+        _lib.call("omniasr_prefill_attention_grouped", _ptr(qp[r0:r0 + rb]), _ptr(kk), _ptr(vv), kk.size(0),
+                  kk.size(2), kk.stride(0), kk.stride(1), kk.stride(2), _ptr(outp[r0:r0 + rb]), rb, heads, width, dim,
+                  float(scale), _lib.BF16, _ptr(ws), ws.numel(), _ptr(status_word(q.device)), _stream(q.device))
+    return outp[:, :width].transpose(1, 2)
 
 
 def _vec(t: torch.Tensor, dtype: torch.dtype, name: str) -> torch.Tensor:
