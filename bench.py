@@ -55,10 +55,13 @@ def peaks() -> dict:
 
 
 def traffic_per_launch(key: str) -> float | None:
-    """DRAM bytes per launch of a workload's dominant kernel from the committed ncu summary, if present."""
+    """DRAM bytes per launch of a workload's dominant kernel from the committed ncu summary, if present. Head
+    geometries other than 32 x 128 have their own lines (suffix `_d<head_dim>`)."""
     path = ROOT / "profiles" / "roofline_traffic.txt"
     if not path.exists():
         return None
+    if D != 128:
+        key = f"{key}_d{D}"
     for line in path.read_text().splitlines():
         if line.startswith(f"{key}="):
             return float(line.split("=", 1)[1])
