@@ -631,10 +631,131 @@ class Gemm(Workload):
         return one, "the output projection (4096 x 4096, 40 rows) in torch on the CPU"
 
 
-WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm)}
+class Select(Workload):
+    """BASELINE config 3 (beam step after the LM head): per input, the best 5 of 5 x 10288 candidates, then the rows
+    follow their parents (pointer / history rows, scores, counts, flags), in place -- beam.py:161-187."""
+
+    name = "select"
+    metric = "beam selection HBM GB/s (8 inputs x 5 beams x 10288 vocab, bf16 log-probs, history 1024, 128 searches)"
+    roof_kernel = "beam_select (one launch per search)"
+    traffic_key = "beam_select_config3_bytes_per_call"
+    S, N, V, G = 8, 5, 10288, 1024
+    SEARCHES = 128  # independent searches per step: 128 x 1.5 MB of state, more than L2
+
+    def __init__(self, device, rank, world, layers):
+        super().__init__(device, rank, world, self.SEARCHES)
+        r = self.S * self.N
+        self.logp = [torch.log_softmax(self.randn(r, self.V).float() * 3, -1).to(torch.bfloat16)
+                     for _ in range(self.layers)]
+        g = torch.Generator(device=device).manual_seed(2000 + rank)
+        dev = device
+        self.state = []
+        for _ in range(self.layers):
+            self.state.append({
+                "score": -torch.rand(r, generator=g, device=dev) * 20,
+                "ended": torch.zeros(r, dtype=torch.bool, device=dev),
+                "count": torch.randint(1, 50, (r,), generator=g, device=dev),
+                "tok": torch.randint(3, self.V, (r,), generator=g, device=dev),
+                "hist": torch.randint(3, self.V, (r, self.G + 1), generator=g, device=dev, dtype=torch.int32),
+                "ptr": (torch.arange(r, device=dev)[:, None] // self.N * self.N
+                        + torch.randint(0, self.N, (r, self.G), generator=g, device=dev)).to(torch.int32),
+                "k_step": torch.full((self.S,), 64, dtype=torch.long, device=dev),
+                "ctx": torch.randint(300, 1801, (self.S,), generator=g, device=dev),
+                "gdone": torch.zeros(self.S, dtype=torch.bool, device=dev),
+            })
+        # logp once + the pointer and history rows read and written + the per-row / per-group scalars
+        self.roof_units = (r * self.V * 2 + 2 * r * (2 * self.G + 1) * 4 + 2 * r * (4 + 1 + 8 + 8)
+                           + 2 * self.S * (8 + 8 + 1))
+        self.step_units = self.roof_units * self.layers
+
+    def layer_in(self, i):
+        return [self.logp[i]]
+
+    def layer(self, i, ev=None):
+        st = self.state[i]
+        if ev:
+            ev[0].record()
+        self.K.beam_select(self.logp[i], st["score"], st["ended"], st["count"], st["tok"], st["hist"], st["ptr"],
+                           st["k_step"], st["ctx"], st["gdone"], self.N, True, 2, 1, 8188)
+        if ev:
+            ev[1].record()
+        return [st["tok"]]
+
+    def config(self):
+        return {"workload": "BASELINE config 3 (beam step): 8 inputs x 5 beams, bf16 log-probabilities over 10288 "
+                            "tokens, length normalisation, history / pointer rows of 1024 positions; 128 independent "
+                            "searches per step (the state advances one step per replay: k_step 64 + replays)",
+                "rows": self.S * self.N, "vocab": self.V, "history": self.G, "searches": self.layers,
+                "bytes_per_step_per_gpu": self.step_units,
+                "l2": f"inputs larger than L2 ({self.layers} distinct searches, {self.step_units / 1e6:.0f} MB)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        from oracle import beam as ob
+
+        rng = np.random.default_rng(0)
+        r = cls.S * cls.N
+        logp = np.log(rng.dirichlet(np.ones(cls.V), r)).astype(np.float32)
+        st = {"score": -rng.random(r).astype(np.float32) * 20, "ended": np.zeros(r, bool),
+              "count": rng.integers(1, 50, r), "tok": rng.integers(3, cls.V, r),
+              "hist": rng.integers(3, cls.V, (r, cls.G + 1)).astype(np.int32),
+              "ptr": (np.arange(r)[:, None] // cls.N * cls.N + rng.integers(0, cls.N, (r, cls.G))).astype(np.int32),
+              "k_step": np.full(cls.S, 64), "ctx": rng.integers(300, 1801, cls.S), "gdone": np.zeros(cls.S, bool)}
+        units = r * cls.V * 2 + 2 * r * (2 * cls.G + 1) * 4
+
+        def one():
+            ob.beam_select(logp, **{k: v.copy() for k, v in st.items()}, beams=cls.N, length_norm=True, eos=2, pad=1,
+                           limit=8188)
+            return units
+
+        return one, "one selection step of the 8 x 5 beams (numpy oracle, fp32 log-probabilities)"
+
+
+WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm, Select)}
 
 
 # ------------------------------------------------------------------------------- the reference's own GPU kernels
+
+
+def reference_beam_select(logp, score, ended, count, tok, hist, ptr, k_step, ctx, gdone, n, length_norm, eos, pad,
+                          limit):
+    """The reference's selection after the LM head as it runs it: the torch operations of BeamDecoder.step_beam,
+    beam.py:161-187, on the first logp.size(0) rows (the reference has no kernel of its own for them)."""
+    r, vocab = logp.shape
+    s = r // n
+    dev = logp.device
+    tok, score, ended, count = tok[:r], score[:r], ended[:r], count[:r]
+    k_step, ctx, gdone = k_step[:s], ctx[:s], gdone[:s]
+    hist, ptr = hist[:r], ptr[:r]
+    rows = torch.arange(r, device=dev)
+    group = rows // n
+    live = ~gdone[group]
+    k = k_step[group]
+    if length_norm:
+        first = count[group * n][:, None]
+        c = count[:, None]
+        cand = torch.where(first > 0, (score[:, None] * c + logp) / (c + 1), score[:, None] + logp)
+    else:
+        cand = score[:, None] + logp
+    cand = cand.masked_fill(ended[:, None], float("-inf"))
+    cand[:, eos] = torch.where(ended, score, cand[:, eos])
+    top, pick = cand.view(s, n * vocab).topk(n, dim=-1, sorted=True)
+    parent = (pick // vocab + torch.arange(s, device=dev)[:, None] * n).view(-1)
+    parent = torch.where(live, parent, rows)
+    new = torch.where(live, (pick % vocab).view(-1), tok)
+    ptr.copy_(ptr[parent])
+    hist.copy_(hist[parent])
+    p_ended, p_score, p_count = ended[parent], score[parent], count[parent]
+    new = torch.where(p_ended, eos, new)
+    hist.scatter_(1, k[:, None], torch.where(live, new, hist.gather(1, k[:, None])[:, 0].long())[:, None]
+                  .to(hist.dtype))
+    score.copy_(torch.where(live & ~p_ended, top.view(-1), p_score))
+    count.copy_(p_count + (live & ~p_ended & (new != pad) & (new != eos)).long())
+    ended.copy_(torch.where(live, new == eos, p_ended))
+    tok.copy_(new)
+    all_ended = ended.view(s, n).all(-1)
+    k_step.copy_(k_step + (~gdone).long())
+    gdone |= all_ended | (ctx - 1 + k_step - 1 >= limit)
 
 
 def reference_gpu_kernels():
@@ -666,7 +787,8 @@ def reference_gpu_kernels():
 
     ns = types.SimpleNamespace(rope_kv=rk.rope_kv, decode_attention=rk.decode_attention,
                                draft_attention=rk.draft_attention, beam_attention=rk.beam_attention,
-                               prefill_attention=prefill_attention, reorder_gather=reorder_gather)
+                               prefill_attention=prefill_attention, reorder_gather=reorder_gather,
+                               beam_select=reference_beam_select)
     return ns, None
 
 

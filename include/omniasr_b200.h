@@ -166,6 +166,23 @@ int omniasr_propose(const int32_t* out, int64_t out_stride, int64_t out_cap, con
                     uint8_t* use_draft, int rows, int tokens, int ngram, int behind, int ahead, const int* reach,
                     int self_window, int self_min, int* status, cudaStream_t stream);
 
+/* Beam search's selection step after the LM head, in place on the first `groups` groups of `beams` rows
+ * (beams <= 16; row r belongs to group r / beams). `logp` [groups * beams, vocab] holds the rows' log-probabilities
+ * (bf16: logp_is_f32 = 0, or fp32; row stride `logp_stride` elements). Per group the best `beams` of its
+ * beams x vocab candidates -- score + logp, or with `length_norm` (when the group's row 0 has counted tokens)
+ * (score * count + logp) / (count + 1), each step rounded to fp32; an ended row offers only `eos` at its score --
+ * in torch.topk(sorted=True)'s order (value descending, equal values by index ascending); then every row of a group
+ * that is not done follows its parent: its `ptr` [rows, ptr_width] and `hist` [rows, hist_width] rows (int32, row
+ * strides in elements) become the parent's, hist[row, k_step[group]] its new token, and score (fp32), count,
+ * ended (one byte), tok (int64) the parent's updated ones; k_step and gdone (int64 / one byte per group, with
+ * `ctx` the group's context length and `limit` the position cap) advance. Bit-exact with the tail of
+ * omniasr_trt/beam.py:161-187 (BeamDecoder.step_beam after the log-softmax). */
+int omniasr_beam_select(const void* logp, int64_t logp_stride, int logp_is_f32, float* score, uint8_t* ended,
+                        int64_t* count, int64_t* tok, int32_t* hist, int64_t hist_stride, int64_t hist_width,
+                        int32_t* ptr, int64_t ptr_stride, int64_t ptr_width, int64_t* k_step, const int64_t* ctx,
+                        uint8_t* gdone, int groups, int beams, int vocab, int length_norm, int64_t eos, int64_t pad,
+                        int64_t limit, int* status, cudaStream_t stream);
+
 /* After a drafted step, in place on rows 0..rows-1: `tokens` [rows, width] were fed (the newest token, then the
  * proposal) and `argmax` [rows, width] is the greedy token after each (int64). A running row (done == 0) keeps
  * argmax 0..n at positions last+1+j of `out` (n: its leading proposed tokens equal to the argmax before them, cut

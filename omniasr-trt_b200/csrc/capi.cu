@@ -7,6 +7,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "beam.cuh"
 #include "gather.cuh"
 #include "omniasr_b200.h"
 #include "prefill.cuh"
@@ -623,6 +624,52 @@ int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, i
   a.eos = eos;
   a.status = status;
   return cuda_status(omni::launch_accept(a, stream), "accept launch");
+}
+
+int omniasr_beam_select(const void* logp, int64_t logp_stride, int logp_is_f32, float* score, uint8_t* ended,
+                        int64_t* count, int64_t* tok, int32_t* hist, int64_t hist_stride, int64_t hist_width,
+                        int32_t* ptr, int64_t ptr_stride, int64_t ptr_width, int64_t* k_step, const int64_t* ctx,
+                        uint8_t* gdone, int groups, int beams, int vocab, int length_norm, int64_t eos, int64_t pad,
+                        int64_t limit, int* status, cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (groups < 0 || beams < 1 || beams > omni::kBeamSelectMaxBeams || vocab < 1)
+    return fail(OMNIASR_ERR_ARGUMENT, "beam_select: groups %d, beams %d (1..%d), vocab %d", groups, beams,
+                omni::kBeamSelectMaxBeams, vocab);
+  if ((int64_t)beams * vocab > INT32_MAX)
+    return fail(OMNIASR_ERR_ARGUMENT, "beam_select: beams x vocab must fit in 31 bits");
+  if (eos < 0 || eos >= vocab) return fail(OMNIASR_ERR_ARGUMENT, "beam_select: eos %lld outside the vocabulary",
+                                           (long long)eos);
+  if (logp_stride < vocab || hist_width < 1 || ptr_width < 0 || hist_stride < hist_width || ptr_stride < ptr_width)
+    return fail(OMNIASR_ERR_ARGUMENT, "beam_select: strides / widths");
+  if (groups == 0) return ok();
+  if (!logp || !score || !ended || !count || !tok || !hist || (!ptr && ptr_width > 0) || !k_step || !ctx || !gdone)
+    return fail(OMNIASR_ERR_ARGUMENT, "beam_select: null pointer");
+  omni::BeamSelectArgs a{};
+  a.logp = logp;
+  a.s_logp = logp_stride;
+  a.logp_f32 = logp_is_f32 ? 1 : 0;
+  a.score = score;
+  a.ended = ended;
+  a.count = count;
+  a.tok = tok;
+  a.hist = hist;
+  a.s_hist = hist_stride;
+  a.hist_w = hist_width;
+  a.ptr = ptr;
+  a.s_ptr = ptr_stride;
+  a.ptr_w = ptr_width;
+  a.k_step = k_step;
+  a.ctx = ctx;
+  a.gdone = gdone;
+  a.groups = groups;
+  a.beams = beams;
+  a.vocab = vocab;
+  a.length_norm = length_norm ? 1 : 0;
+  a.eos = eos;
+  a.pad = pad;
+  a.limit = limit;
+  a.status = status;
+  return cuda_status(omni::launch_beam_select(a, stream), "beam_select launch");
 }
 
 size_t omniasr_decode_gemm_workspace(int rows, int n, int k, int mode) {

@@ -6,8 +6,10 @@ After :func:`install`, ``import omniasr_trt.kernels`` (and the ``from . import k
 control kernels ``propose`` / ``accept`` -- are this package's CUDA kernels, and the prefill's causal
 ``F.scaled_dot_product_attention`` in ``decode.py`` (decode.py:171) runs
 :func:`omniasr_b200.kernels.prefill_attention`. No Triton kernel of the reference remains on these decoders' path.
-Nothing else of the reference changes: its decoders, CUDA-graph capture, ``OmniASRLLM.transcribe`` and
-``compat.Pipeline`` run unchanged on top.
+The beam decoder's selection after the LM head (beam.py:161-187: candidates, per-group top-k, the pointer / history
+reorder and the state updates, some thirty small torch kernels) runs as one kernel,
+:func:`omniasr_b200.kernels.beam_select`, through :func:`_beam_step`. Nothing else of the reference changes: its
+decoders, CUDA-graph capture, ``OmniASRLLM.transcribe`` and ``compat.Pipeline`` run unchanged on top.
 """
 
 from __future__ import annotations
@@ -43,6 +45,52 @@ class _Functional(types.ModuleType):
                                                           is_causal=is_causal, scale=scale, **kw)
 
 
+def _beam_step(self, s: int, ckeys: int, gkeys: int) -> None:
+    """``BeamDecoder.step_beam`` (beam.py:127-187) with its selection as one kernel.
+
+    The step up to the log-probabilities is the reference's own sequence of operations (beam.py:130-160: the pointer
+    of the token fed now, then per layer the QKV product, ``rope_kv``, the beam attention, the output projection and
+    the SwiGLU FFN, then the final norm, the LM head and the log-softmax) -- it must be, for the same tokens; the
+    candidates, per-group top-k, parents and reorder that follow are :func:`kernels.beam_select`. Shapes and dtypes
+    the kernel does not take (the PyTorch path, an fp64 model, more than 16 beams) run the reference's own method."""
+    import torch
+    import torch.nn.functional as F
+
+    from . import kernels as ours
+
+    if not self.fused or self.score.dtype != torch.float32 or self.dtype not in (torch.bfloat16, torch.float32) \
+            or self.beams > 16:
+        return _beam_step.reference(self, s, ckeys, gkeys)
+    m, n = self.m, self.beams
+    r = s * n
+    rows = torch.arange(r, device=self.device)
+    gdone, ctx = self.gdone[:s], self.ctx[:s]
+    live = ~gdone[self.group[:r]]
+    k = self.k_step[:s][self.group[:r]]  # the token fed now was chosen at step k - 1
+    pos = ctx[self.group[:r]] - 1 + k  # its input position
+    j = (k - 1).clamp(min=0)  # its generated-cache position
+    ctx_len = torch.where(gdone, 0, ctx)
+    gen_len = torch.where(live, k, 0)
+    ptr = self.ptr[:r]
+    kept = ptr.gather(1, j[:, None])[:, 0].long()
+    ptr.scatter_(1, j[:, None], torch.where(live, rows, kept)[:, None].to(ptr.dtype))
+    h = m.text_frontend.weight[self.tok[:r]]
+    for i, layer in enumerate(m.llama_decoder.layers):
+        qkv_w, out_w, gi_w, ffo_w = self.layers[i]
+        qkv = layer.self_attn_layer_norm(h) @ qkv_w.t()
+        q = ours.rope_kv(qkv, m.rope, pos, self.kg[i], self.vg[i], self.heads, cache_pos=j)
+        o = self.attention(i, q, ctx_len, gen_len, s, ckeys, gkeys).reshape(r, -1)
+        h = torch.addmm(h, o, out_w.t())
+        gate, inner = (layer.ffn_layer_norm(h) @ gi_w.t()).chunk(2, -1)
+        h = torch.addmm(h, inner * F.silu(gate), ffo_w.t())
+    logp = F.log_softmax(m.final_proj(m.llama_decoder.layer_norm(h)), dim=-1)
+    ours.beam_select(logp, self.score, self.ended, self.count, self.tok, self.hist, self.ptr, self.k_step, self.ctx,
+                     self.gdone, n, self.length_norm, EOS, PAD, LIMIT)
+
+
+EOS, PAD, LIMIT = 2, 1, 8188  # set from the reference's llm / decode modules by install()
+
+
 def install(package: str = "omniasr_trt") -> types.ModuleType:
     """Swaps ``<package>.kernels`` for a module with this package's path functions; returns that module."""
     from . import kernels as ours
@@ -69,4 +117,11 @@ def install(package: str = "omniasr_trt") -> types.ModuleType:
     decode = importlib.import_module(f"{package}.decode")  # its prefill attention (decode.py:171)
     if not isinstance(decode.F, _Functional):
         decode.F = _Functional(ours.prefill_attention)
+    beam = importlib.import_module(f"{package}.beam")  # its selection after the LM head (beam.py:161-187)
+    llm = importlib.import_module(f"{package}.llm")
+    global EOS, PAD, LIMIT
+    EOS, PAD, LIMIT = llm.EOS, llm.PAD, decode.LIMIT
+    if beam.BeamDecoder.step_beam is not _beam_step:
+        _beam_step.reference = beam.BeamDecoder.step_beam
+        beam.BeamDecoder.step_beam = _beam_step
     return merged

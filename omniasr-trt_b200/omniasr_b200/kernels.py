@@ -354,6 +354,36 @@ def accept(tokens: torch.Tensor, nxt: torch.Tensor, out: torch.Tensor, tok: torc
               int(eos), _ptr(status_word(out.device)), _stream(out.device))
 
 
+def beam_select(logp: torch.Tensor, score: torch.Tensor, ended: torch.Tensor, count: torch.Tensor, tok: torch.Tensor,
+                hist: torch.Tensor, ptr: torch.Tensor, k_step: torch.Tensor, ctx: torch.Tensor, gdone: torch.Tensor,
+                beams: int, length_norm: bool, eos: int, pad: int, limit: int) -> None:
+    """Beam search's selection step after the LM head, in place: ``logp`` [S * beams, V] (bf16 or fp32) selects, per
+    group of ``beams`` rows, the group's best ``beams`` candidates over beams x V and every row of a group that is
+    not done follows its parent. State: ``score`` [R] fp32, ``ended`` [R] bool, ``count`` / ``tok`` [R] int64,
+    ``hist`` [R, G + 1] / ``ptr`` [R, G] int32 (unit inner stride), ``k_step`` / ``ctx`` [S] int64, ``gdone`` [S]
+    bool, R >= S * beams. Bit-exact with BeamDecoder.step_beam after its log-softmax (beam.py:161-187)."""
+    rows, vocab = logp.shape
+    groups = rows // beams
+    if rows != groups * beams:
+        raise ValueError("beam_select: logp rows must be groups x beams")
+    if logp.dtype not in (torch.bfloat16, torch.float32) or logp.stride(1) != 1:
+        raise ValueError("beam_select: logp must be bf16 or fp32 with unit inner stride")
+    if groups == 0:
+        return
+    _vec(score, torch.float32, "score")
+    _vec(ended, torch.bool, "ended")
+    for t, name in ((count, "count"), (tok, "tok"), (k_step, "k_step"), (ctx, "ctx")):
+        _vec(t, torch.int64, name)
+    _vec(gdone, torch.bool, "gdone")
+    for t, name in ((hist, "hist"), (ptr, "ptr")):
+        if t.dtype != torch.int32 or t.dim() != 2 or (t.size(1) > 1 and t.stride(1) != 1):
+            raise ValueError(f"beam_select: {name} must be int32 [rows, width] with unit inner stride")
+    _lib.call("omniasr_beam_select", _ptr(logp), logp.stride(0), int(logp.dtype == torch.float32), _ptr(score),
+              _ptr(ended), _ptr(count), _ptr(tok), _ptr(hist), hist.stride(0), hist.size(1), _ptr(ptr), ptr.stride(0),
+              ptr.size(1), _ptr(k_step), _ptr(ctx), _ptr(gdone), groups, beams, vocab, int(bool(length_norm)),
+              int(eos), int(pad), int(limit), _ptr(status_word(logp.device)), _stream(logp.device))
+
+
 GEMM_MODES = {"store": 0, "residual": 1, "swiglu": 2}
 _GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters zero
 _GEMM_WS_RETIRED: list = []  # outgrown workspaces, kept alive for CUDA graphs that captured them

@@ -178,3 +178,42 @@ def test_accept_oracle_matches_reference_golden():
         for got, k in zip(state, ("out", "tok", "last", "done", "draft_next")):
             assert np.array_equal(got, d[p + k + "_after"]), f"width {int(width)}: {k}"
         assert not np.array_equal(d[p + "last"], d[p + "last_after"])  # the step advanced some rows
+
+
+BEAM_FIELDS = ("score", "ended", "count", "tok", "hist", "ptr", "k_step", "ctx", "gdone")
+
+
+def _beam_record(z, i):
+    beams, ln = (int(v) for v in z[f"{i}_meta"])
+    state = {k: z[f"{i}_in_{k}"].copy() for k in BEAM_FIELDS}
+    want = {k: z[f"{i}_out_{k}"] for k in BEAM_FIELDS}
+    return z[f"{i}_logp"], state, want, beams, bool(ln)
+
+
+def test_beam_select_oracle_matches_reference_golden():
+    """The selection tail of the reference's BeamDecoder.step_beam (beam.py:161-187), recorded step by step from
+    its own PyTorch path (tests/golden/make_beam_golden.py): the numpy restatement gives every state field exactly."""
+    from oracle import beam
+
+    z = np.load(GOLDEN / "beam_select.npz")
+    n = int(z["n"])
+    assert n >= 90
+    seen_ended = seen_done = seen_norm = 0
+    for i in range(n):
+        logp, st, want, beams, ln = _beam_record(z, i)
+        seen_ended += bool(st["ended"].any())
+        seen_done += bool(st["gdone"].any())
+        seen_norm += ln
+        beam.beam_select(logp, **st, beams=beams, length_norm=ln, eos=2, pad=1, limit=8188)
+        for k in BEAM_FIELDS:
+            assert np.array_equal(st[k], want[k]), (i, k)
+    assert seen_ended and seen_done and seen_norm  # the golden covers ended rows, done groups, length_norm
+
+
+def test_beam_select_oracle_tie_order():
+    """Equal candidates order by flat index (value descending first), as torch.topk orders them on a CUDA tensor."""
+    from oracle import beam
+
+    v = np.array([1.0, 3.0, 3.0, 2.0, 3.0, -0.0, 0.0, 3.0], dtype=np.float32)
+    assert beam.topk_order(v, 5).tolist() == [1, 2, 4, 7, 3]
+    assert beam.topk_order(np.array([0.0, -0.0, 0.0], dtype=np.float32), 3).tolist() == [0, 1, 2]
