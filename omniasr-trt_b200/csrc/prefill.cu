@@ -28,6 +28,13 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <array>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <queue>
+#include <vector>
+
 #include "attention.cuh"
 #include "prefill.cuh"
 #include "tc.cuh"
@@ -195,6 +202,30 @@ OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
   h = bh % p.heads;
 }
 
+// A precomputed assignment of units to CTAs (kernel parameters): CTA c runs unit[start[c]] .. unit[start[c+1] - 1]
+// in that order. The host builds it by list scheduling in the order unit_of numbers the units (each unit goes to
+// the CTA that is free first, by a cost of its key tiles plus a unit's fixed cost), which keeps the CTAs' end times
+// within about 1% where a round-robin assignment spreads them by 7-8% (config 4); the units a CTA runs at one time
+// still belong to about one group. Shapes with more units than it holds, or grids larger than it covers, run
+// round-robin (u = c, c + grid, ...).
+constexpr int kSchedUnits = 4096;
+constexpr int kSchedCtas = 160;
+struct Sched {
+  int on;
+  uint16_t start[kSchedCtas + 1];
+  uint16_t unit[kSchedUnits];
+};
+
+// The CTA's n-th unit, or -1 past its last.
+OMNI_DEV int cta_unit(const Sched& s, int units, int n) {
+  if (!s.on) {
+    const int u = (int)blockIdx.x + n * (int)gridDim.x;
+    return u < units ? u : -1;
+  }
+  const int k = (int)s.start[blockIdx.x] + n;
+  return k < (int)s.start[blockIdx.x + 1] ? (int)s.unit[k] : -1;
+}
+
 // The CTA's control block: barriers, the row maxima exchanged between the softmax warpgroups, the unit's row sums
 // for the epilogue, flags. One static struct, padded to 1024 bytes, so that the dynamic tile ring after it starts
 // 1024-aligned (the kernel checks, and reports status bit 4 otherwise).
@@ -224,7 +255,7 @@ OMNI_DEV bool sync_or(int id, int count, bool pred) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+                   const __grid_constant__ CUtensorMap vmap, const Params p, const __grid_constant__ Sched sched) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ Ctl ctl;
   uint64_t *k_full = ctl.k_full, *k_empty = ctl.k_empty, *v_full = ctl.v_full, *v_empty = ctl.v_empty;
@@ -298,7 +329,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       int tile = 0;
-      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
+      for (int n = 0, u; (u = cta_unit(sched, units, n)) >= 0 && !abort_flag; ++n) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
         for (int kt = 0; kt <= qt && !abort_flag; ++kt, ++tile) {
@@ -324,7 +355,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t qdesc0 = smem_desc(smem_addr(smem + Q_OFF), 16, 1024, kLayoutSw128);
       int tile = 0, nunit = 0, sb = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
+      for (int u; (u = cta_unit(sched, units, nunit)) >= 0 && ok && !abort_flag; ++nunit) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
         const int qslot = nunit % QS;
@@ -364,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t vdesc0 = smem_desc(smem_addr(smem + V_OFF), BOX, 1024, kLayoutSw128);
       int tile = 0, nunit = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok && !abort_flag; u += gridDim.x, ++nunit) {
+      for (int u; (u = cta_unit(sched, units, nunit)) >= 0 && ok && !abort_flag; ++nunit) {
         int b, h, qt;
         unit_of(p, u, b, h, qt);
         for (int kt = 0; kt <= qt; ++kt, ++tile) {
@@ -412,7 +443,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t col_o = tbase + lane_off + COL_O + x * DW;  // this warpgroup's head dims of O (rescale)
     int tile = 0, nunit = 0;
     bool quit = false;
-    for (int u = blockIdx.x; u < units && !quit; u += gridDim.x, ++nunit) {
+    for (int u; (u = cta_unit(sched, units, nunit)) >= 0 && !quit; ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
       float m = -INFINITY, l = 0.f;
@@ -545,15 +576,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     if (q_loader) {
       prefetch_tmap(&qmap);
-      for (int n = 0; n < QS && (int)blockIdx.x + n * (int)gridDim.x < units; ++n) load_q(n, blockIdx.x + n * gridDim.x);
+      for (int n = 0, u; n < QS && (u = cta_unit(sched, units, n)) >= 0; ++n) load_q(n, u);
     }
     int nunit = 0;
-    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++nunit) {
+    for (int u; (u = cta_unit(sched, units, nunit)) >= 0 && !abort_flag; ++nunit) {
       int b, h, qt;
       unit_of(p, u, b, h, qt);
-      if (q_loader && u + QS * (int)gridDim.x < units) {
+      const int ahead = q_loader ? cta_unit(sched, units, nunit + QS) : -1;
+      if (ahead >= 0) {
         if (!wait(&q_empty[nunit % QS], (nunit / QS) & 1)) break;
-        load_q(nunit + QS, u + QS * gridDim.x);
+        load_q(nunit + QS, ahead);
       }
       if (!wait(&o_ready, nunit & 1)) break;
       if (!wait(&l_full, nunit & 1)) break;
@@ -625,6 +657,49 @@ int prefill_group(int bh_count) {
   return g < bh_count ? g : bh_count;
 }
 
+// Fixed cost of a unit in key tiles (measured: a unit's first tile takes about 1.6 tiles' time).
+constexpr float kUnitCost = 0.6f;
+
+// The list schedule of `units` units (unit_of's numbering) over `grid` CTAs, cached per shape.
+const Sched* schedule(int batch, int heads, int qtiles, int group, int grid) {
+  static const bool off = [] {  // OMNIASR_PREFILL_SCHED=0: round-robin (for comparisons)
+    const char* e = getenv("OMNIASR_PREFILL_SCHED");
+    return e && atoi(e) == 0;
+  }();
+  const int units = batch * heads * qtiles;
+  if (off || units > kSchedUnits || grid > kSchedCtas) return nullptr;
+  static std::mutex mu;
+  static std::map<std::array<int, 5>, std::unique_ptr<Sched>> cache;
+  const std::array<int, 5> key{batch, heads, qtiles, group, grid};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second.get();
+  auto s = std::make_unique<Sched>();
+  std::vector<std::vector<uint16_t>> lists(grid);
+  using Slot = std::pair<float, int>;  // (time the CTA is free, CTA)
+  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> free_at;
+  for (int c = 0; c < grid; ++c) free_at.push({0.f, c});
+  const int bh_count = batch * heads;
+  for (int u = 0; u < units; ++u) {
+    const int per_group = group * qtiles;  // unit_of's numbering, on the host
+    const int g0 = (u / per_group) * group;
+    const int gsize = std::min(group, bh_count - g0);
+    const int qt = qtiles - 1 - (u - g0 * qtiles) / gsize;
+    const Slot c = free_at.top();
+    free_at.pop();
+    lists[c.second].push_back((uint16_t)u);
+    free_at.push({c.first + (float)(qt + 1) + kUnitCost, c.second});
+  }
+  s->on = 1;
+  int k = 0;
+  for (int c = 0; c < grid; ++c) {
+    s->start[c] = (uint16_t)k;
+    for (uint16_t u : lists[c]) s->unit[k++] = u;
+  }
+  s->start[grid] = (uint16_t)k;
+  return cache.emplace(key, std::move(s)).first->second.get();
+}
+
 bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t w, int64_t sb, int64_t sh,
               int64_t sw) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
@@ -680,7 +755,14 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   int grid = device_sm_count();
   if (grid > units) grid = units;
   if (grid <= 0) return cudaSuccess;
-  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p);
+  static const Sched round_robin = [] {
+    Sched r{};
+    r.on = 0;
+    return r;
+  }();
+  const Sched* sched = schedule(p.batch, p.heads, p.qtiles, p.group, grid);
+  return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p,
+                          sched ? *sched : round_robin);
 }
 
 }  // namespace omni
