@@ -118,10 +118,10 @@ int omniasr_beam_attention(const void* q, const void* kc, const void* vc, int64_
                            void* out, int groups, int beams, int heads, int dim, int ctx_keys, float scale, int dtype,
                            void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
 
-/* Causal prefill attention (bf16, head_dim 128): out[b, h, w] = softmax(q[b, h, w] . k[b, h, :w+1]^T * scale)
- * . v[b, h, :w+1] for every position w < width. q, k, v and out are [batch, heads, width, 128] given by base
+/* Causal prefill attention (bf16, head_dim 128 or 512): out[b, h, w] = softmax(q[b, h, w] . k[b, h, :w+1]^T *
+ * scale) . v[b, h, :w+1] for every position w < width. q, k, v and out are [batch, heads, width, dim] given by base
  * pointer and (row, head, position) element strides (k and v are typically views of the KV cache; out may be a
- * [batch, width, heads, 128] buffer seen through its strides). Replaces the reference's prefill
+ * [batch, width, heads, dim] buffer seen through its strides). Replaces the reference's prefill
  * F.scaled_dot_product_attention(q, k, v, is_causal=True), omniasr_trt/decode.py:171. */
 int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_stride_head, int64_t q_stride_pos,
                               const void* k, int64_t k_stride_row, int64_t k_stride_head, int64_t k_stride_pos,

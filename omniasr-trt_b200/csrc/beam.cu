@@ -14,15 +14,20 @@
 // read before any is written, column block by column block), then the row's new token goes into hist at the
 // group's step, and score, count, ended, tok, k_step and gdone are updated as the reference updates them.
 
+#include <cooperative_groups.h>
+
 #include "beam.cuh"
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace omni {
 
 namespace {
 
-constexpr int kThreads = 1024;  // 64 registers a thread at most
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kCluster = 8;  // CTAs per group: each scans an eighth of the candidates and copies an eighth of the rows
 
 // A candidate's sort key: a larger key comes first. The value's bits are mapped to an order-preserving unsigned
 // integer (-0 counted as +0, every NaN as the largest value, as a comparison-based top-k sees them); the low word
@@ -70,19 +75,70 @@ OMNI_DEV void warp_merge(uint64_t (&best)[NB], uint64_t* out) {
   }
 }
 
+// The order torch.topk(sorted=True) returns a CUDA tensor's k <= 32 best in (the reference calls it on the group's
+// beams x vocab candidates), on the k keys `best` holds in (value descending, index ascending) order: its selection
+// lists the values above the k-th best value, then those equal to it, each in index order, and its sort of those k is
+// a bitonic network over 32 slots (the unused slots last) that exchanges two entries unless the first is the larger,
+// so equal values end up in an order fixed by their slots. One thread; the network's stages in sequence.
+__device__ __noinline__ void torch_order(uint64_t* best, int n) {
+  constexpr int P = 32;
+  uint32_t kv[P], ix[P];
+  bool ok[P];
+  const uint32_t kth = (uint32_t)(best[n - 1] >> 32);
+  int m = 0;
+  for (int pass = 0; pass < 2; ++pass) {  // above the k-th value, then equal to it; each by index
+    const int first = m;
+    for (int j = 0; j < n; ++j) {
+      const uint32_t hi = (uint32_t)(best[j] >> 32);
+      if (pass == 0 ? hi <= kth : hi != kth) continue;
+      kv[m] = hi;
+      ix[m] = key_index(best[j]);
+      int i = m++;
+      while (i > first && ix[i - 1] > ix[i]) {  // insertion by index
+        const uint32_t tk = kv[i], ti = ix[i];
+        kv[i] = kv[i - 1];
+        ix[i] = ix[i - 1];
+        kv[i - 1] = tk;
+        ix[i - 1] = ti;
+        --i;
+      }
+    }
+  }
+  for (int i = 0; i < P; ++i) ok[i] = i < n;
+  for (int i = n; i < P; ++i) kv[i] = ix[i] = 0;
+  auto exchange = [&](int x, int y, bool dir) {
+    const bool s = (kv[x] > kv[y] && ok[x]) || !ok[y];
+    if (s == dir) {
+      const uint32_t tk = kv[x], ti = ix[x];
+      const bool tv = ok[x];
+      kv[x] = kv[y];
+      ix[x] = ix[y];
+      ok[x] = ok[y];
+      kv[y] = tk;
+      ix[y] = ti;
+      ok[y] = tv;
+    }
+  };
+  for (int size = 2; size < P; size *= 2)
+    for (int stride = size / 2; stride > 0; stride /= 2)
+      for (int t = 0; t < P / 2; ++t) exchange(2 * t - (t & (stride - 1)), 2 * t - (t & (stride - 1)) + stride,
+                                               (t & (size / 2)) != 0);
+  for (int stride = P / 2; stride > 0; stride /= 2)
+    for (int t = 0; t < P / 2; ++t) exchange(2 * t - (t & (stride - 1)), 2 * t - (t & (stride - 1)) + stride, false);
+  for (int j = 0; j < n; ++j) best[j] = ((uint64_t)kv[j] << 32) | (uint32_t)~ix[j];
+}
+
 struct Row {
   float score;
+  float c, c1;  // count and count + 1 as floats (torch converts the int64 operands to float32)
   int64_t count;
   uint8_t ended;
 };
 
-// One candidate's value, as beam.py:163-170 computes it.
-OMNI_DEV float cand_value(const BeamSelectArgs& a, const Row& r, int64_t first, float lp, int t) {
+// One candidate's value, as beam.py:163-170 computes it (`norm`: length normalisation on for the group).
+OMNI_DEV float cand_value(const BeamSelectArgs& a, const Row& r, bool norm, float lp, int t) {
   if (r.ended) return t == a.eos ? r.score : -INFINITY;
-  if (a.length_norm && first > 0) {
-    const float c = __ll2float_rn(r.count);
-    return __fdiv_rn(__fadd_rn(__fmul_rn(r.score, c), lp), __ll2float_rn(r.count + 1));
-  }
+  if (norm) return __fdiv_rn(__fadd_rn(__fmul_rn(r.score, r.c), lp), r.c1);
   return __fadd_rn(r.score, lp);
 }
 
@@ -90,34 +146,43 @@ OMNI_DEV float to_float(float x) { return x; }
 OMNI_DEV float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 template <int NB, typename T, int E>
-__global__ void __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectArgs a) {
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectArgs a) {
   __shared__ Row rows[kBeamSelectMaxBeams];
   __shared__ uint64_t warp_best[kWarps][NB];
+  __shared__ uint64_t cta_best[NB];  // read by the other CTAs of the cluster
   __shared__ uint64_t group_best[NB];
   __shared__ int parent_s[kBeamSelectMaxBeams];
   __shared__ uint8_t ended_new[kBeamSelectMaxBeams];
 
-  const int g = blockIdx.x, n = a.beams, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = (int)cluster.block_rank();
+  const int g = blockIdx.x / kCluster, n = a.beams, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row0 = (int64_t)g * n;
   const bool live = a.gdone[g] == 0;
   const int64_t k = a.k_step[g];
   if (tid < n) {
-    rows[tid].score = a.score[row0 + tid];
-    rows[tid].count = a.count[row0 + tid];
-    rows[tid].ended = a.ended[row0 + tid];
+    Row r;
+    r.score = a.score[row0 + tid];
+    r.count = a.count[row0 + tid];
+    r.ended = a.ended[row0 + tid];
+    r.c = __ll2float_rn(r.count);
+    r.c1 = __ll2float_rn(r.count + 1);
+    rows[tid] = r;
   }
   __syncthreads();
 
   if (live) {
-    // ---------------------------------------------------------------- top-k over the group's beams x vocab
-    const int64_t first = rows[0].count;
+    // ---------------------------------------------------------------- top-k over this CTA's share of the candidates
+    const bool norm = a.length_norm && rows[0].count > 0;
     uint64_t best[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) best[j] = 0;
     const int per_row = a.vocab / E;  // E divides vocab on the vector path
     const int total = n * per_row;
-    int b = tid / per_row, t = (tid - b * per_row) * E;
-    for (int vi = tid; vi < total; vi += kThreads) {
+    const int share = (total + kCluster - 1) / kCluster;
+    const int v0 = q * share, v1 = min(total, v0 + share);
+    int b = (v0 + tid) / per_row, t = (v0 + tid - b * per_row) * E;
+    for (int vi = v0 + tid; vi < v1; vi += kThreads) {
       const Row r = rows[b];
       const T* src = reinterpret_cast<const T*>(a.logp) + (row0 + b) * a.s_logp + t;
       T vals[E];
@@ -129,7 +194,7 @@ __global__ void __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectA
       }
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        insert(best, cand_key(cand_value(a, r, first, to_float(vals[e]), t + e), (uint32_t)(b * a.vocab + t + e)));
+        insert(best, cand_key(cand_value(a, r, norm, to_float(vals[e]), t + e), (uint32_t)(b * a.vocab + t + e)));
       t += kThreads * E;
       while (t >= a.vocab) {
         t -= a.vocab;
@@ -141,10 +206,24 @@ __global__ void __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectA
     if (warp == 0) {
 #pragma unroll
       for (int j = 0; j < NB; ++j) best[j] = lane < kWarps ? warp_best[lane][j] : 0;
+      warp_merge(best, cta_best);
+    }
+  }
+  cluster.sync();  // every CTA's list is complete
+  if (live) {
+    // Every CTA merges the cluster's lists itself (the same result everywhere), reading the others' shared memory.
+    if (warp == 0) {
+      uint64_t best[NB];
+      const uint64_t* peer = lane < kCluster ? cluster.map_shared_rank(cta_best, lane) : nullptr;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) best[j] = peer ? peer[j] : 0;
       warp_merge(best, group_best);
     }
-    __syncthreads();
   }
+  cluster.sync();  // the lists have been read: a CTA may leave once it is done
+
+  if (live && tid == 0) torch_order(group_best, n);
+  __syncthreads();
 
   // -------------------------------------------------------------------- parents, new tokens (beam.py:172-178)
   int64_t new_tok = 0;
@@ -160,9 +239,8 @@ __global__ void __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectA
       par = (int)(idx / (uint32_t)a.vocab);
       const int tv = (int)(idx - (uint32_t)par * (uint32_t)a.vocab);
       new_tok = tv;
-      const Row& pr = rows[par];
       const T* src = reinterpret_cast<const T*>(a.logp) + (row0 + par) * a.s_logp + tv;
-      top = cand_value(a, pr, rows[0].count, to_float(*src), tv);
+      top = cand_value(a, rows[par], a.length_norm && rows[0].count > 0, to_float(*src), tv);
     } else {
       new_tok = a.tok[row];
     }
@@ -178,34 +256,40 @@ __global__ void __launch_bounds__(kThreads) beam_select_kernel(const BeamSelectA
   __syncthreads();
 
   // -------------------------------------------------------------------- ptr / hist rows follow their parents
+  // CTA q of the cluster copies columns [q, q + 1) x width / kCluster of every row: the column ranges are disjoint,
+  // so within a range all the group's parent values are read before any is written (one CTA, a barrier between).
   if (live) {
     for (int pass = 0; pass < 2; ++pass) {
       int32_t* base = pass == 0 ? a.ptr : a.hist;
       const int64_t stride = pass == 0 ? a.s_ptr : a.s_hist, width = pass == 0 ? a.ptr_w : a.hist_w;
-      for (int64_t c0 = 0; c0 < width; c0 += kThreads) {
+      const int64_t span = (width + kCluster - 1) / kCluster;
+      const int64_t cbeg = q * span, cend = min(width, cbeg + span);
+      for (int64_t c0 = cbeg; c0 < cend; c0 += kThreads) {
         const int64_t c = c0 + tid;
         int32_t v[NB];  // n <= NB
 #pragma unroll
         for (int j = 0; j < NB; ++j)
-          if (j < n && c < width) v[j] = base[(row0 + parent_s[j]) * stride + c];
+          if (j < n && c < cend) v[j] = base[(row0 + parent_s[j]) * stride + c];
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < NB; ++j)
-          if (j < n && c < width && parent_s[j] != j) base[(row0 + j) * stride + c] = v[j];
+          if (j < n && c < cend && parent_s[j] != j) base[(row0 + j) * stride + c] = v[j];
         __syncthreads();
+      }
+      if (pass == 1 && tid < n) {  // the new token at the group's step, by the CTA whose columns hold it
+        if (k >= 0 && k < a.hist_w) {
+          if (k >= cbeg && k < cend) a.hist[(row0 + tid) * a.s_hist + k] = (int32_t)new_tok;
+        } else if (q == 0) {
+          raise_status(a.status, kStatusIndex);
+        }
       }
     }
   }
 
   // -------------------------------------------------------------------- the rows' new state (beam.py:179-187)
+  if (q != 0) return;
   if (tid < n) {
     const int64_t row = row0 + tid;
-    if (live) {
-      if (k >= 0 && k < a.hist_w)
-        a.hist[row * a.s_hist + k] = (int32_t)new_tok;
-      else
-        raise_status(a.status, kStatusIndex);
-    }
     a.score[row] = new_score;
     a.count[row] = new_count;
     a.ended[row] = new_ended;
@@ -225,9 +309,9 @@ cudaError_t launch_t(const BeamSelectArgs& a, cudaStream_t stream) {
   constexpr int E = 16 / sizeof(T);
   const bool vec = a.vocab % E == 0 && a.s_logp % E == 0 && reinterpret_cast<uintptr_t>(a.logp) % 16 == 0;
   if (vec)
-    beam_select_kernel<NB, T, E><<<a.groups, kThreads, 0, stream>>>(a);
+    beam_select_kernel<NB, T, E><<<a.groups * kCluster, kThreads, 0, stream>>>(a);
   else
-    beam_select_kernel<NB, T, 1><<<a.groups, kThreads, 0, stream>>>(a);
+    beam_select_kernel<NB, T, 1><<<a.groups * kCluster, kThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -426,8 +426,9 @@ int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_str
                               int batch, int heads, int width, int dim, float scale, int dtype, int* status,
                               cudaStream_t stream) {
   const char* name = "prefill_attention";
-  if (dtype != OMNIASR_BF16 || dim != 128)
-    return fail(OMNIASR_ERR_UNSUPPORTED, "%s: bf16 with head_dim 128 only (dtype %d, head_dim %d)", name, dtype, dim);
+  if (dtype != OMNIASR_BF16 || (dim != 128 && dim != 512))
+    return fail(OMNIASR_ERR_UNSUPPORTED, "%s: bf16 with head_dim 128 or 512 only (dtype %d, head_dim %d)", name, dtype,
+                dim);
   if (int e = check_device()) return e;
   if (batch < 0 || heads <= 0 || width < 0) return fail(OMNIASR_ERR_ARGUMENT, "%s: shape", name);
   if (batch == 0 || width == 0) return ok();
@@ -461,7 +462,7 @@ int omniasr_prefill_attention(const void* q, int64_t q_stride_row, int64_t q_str
   a.width = width;
   a.scale = scale;
   a.status = status;
-  return cuda_status(omni::launch_prefill(a, stream), "prefill launch");
+  return cuda_status(dim == 512 ? omni::launch_prefill_wide(a, stream) : omni::launch_prefill(a, stream), "prefill launch");
 }
 
 size_t omniasr_prefill_grouped_workspace(int batch, int heads, int width, int dim) {

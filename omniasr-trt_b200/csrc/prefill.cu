@@ -37,11 +37,14 @@
 
 #include "attention.cuh"
 #include "prefill.cuh"
+#include "prefill_common.cuh"
 #include "tc.cuh"
 #include "trace.cuh"
 
 namespace omni {
 namespace prefill {
+
+using namespace pfx;
 
 constexpr int D = 128;
 constexpr int BM = 128;  // queries per tile
@@ -81,149 +84,8 @@ struct Params {
   int* status;
 };
 
-// D (TMEM) = A (TMEM) x B (smem) [+ D]; issued by one thread.
-OMNI_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-OMNI_DEV void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 32 columns of this thread's lane without waiting (complete after tmem_wait_ld()).
-OMNI_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-
-// 2^x on the FMA and integer pipes, for x <= 127 (the softmax's arguments are at most 8): x = j + f with j the
-// nearest integer (the 1.5 * 2^23 addition leaves j in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f from a
-// cubic fitted here for relative error on [-0.5, 0.5] (7.5e-5 at most, far below bf16's 2^-9); 2^j added to the
-// exponent field. x is clamped to -126 (2^-126 or a denormal below it: zero to a probability), so that the exponent
-// field never wraps. Used for part of the probabilities, so that the special-function unit, which forms the others
-// with ex2, is not the only pipe the exponentials load.
-OMNI_DEV float ex2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float q = fmaf(fmaf(fmaf(0.055174146f, f, 0.24261758f), f, 0.69326109f), f, 0.99992758f);
-  return __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
-}
-
-// Packed pairs of floats for the f32x2 forms of fma / add (one instruction for two elements on the FMA pipe).
-OMNI_DEV uint64_t f2_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-OMNI_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
-OMNI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-OMNI_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-OMNI_DEV float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Two floats rounded to bf16 and packed (lo in the low half).
-OMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-OMNI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-OMNI_DEV void tmem_st32(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-OMNI_DEV void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-OMNI_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// Unit u -> (b, h, qt). The (row, head) pairs are taken in groups of p.group, and a group's units heaviest query
-// tile first: the CTAs running at one time then read the K/V of about one group, which stays in L2.
 OMNI_DEV void unit_of(const Params& p, int u, int& b, int& h, int& qt) {
-  const int bh_count = p.batch * p.heads;
-  const int per_group = p.group * p.qtiles;
-  const int g0 = (u / per_group) * p.group;
-  const int gsize = min(p.group, bh_count - g0);
-  const int r = u - g0 * p.qtiles;
-  qt = p.qtiles - 1 - r / gsize;
-  const int bh = g0 + r % gsize;
-  b = bh / p.heads;
-  h = bh % p.heads;
-}
-
-// A precomputed assignment of units to CTAs (kernel parameters): CTA c runs unit[start[c]] .. unit[start[c+1] - 1]
-// in that order. The host builds it by list scheduling in the order unit_of numbers the units (each unit goes to
-// the CTA that is free first, by a cost of its key tiles plus a unit's fixed cost), which keeps the CTAs' end times
-// within about 1% where a round-robin assignment spreads them by 7-8% (config 4); the units a CTA runs at one time
-// still belong to about one group. Shapes with more units than it holds, or grids larger than it covers, run
-// round-robin (u = c, c + grid, ...).
-constexpr int kSchedUnits = 4096;
-constexpr int kSchedCtas = 160;
-struct Sched {
-  int on;
-  uint16_t start[kSchedCtas + 1];
-  uint16_t unit[kSchedUnits];
-};
-
-// The CTA's n-th unit, or -1 past its last.
-OMNI_DEV int cta_unit(const Sched& s, int units, int n) {
-  if (!s.on) {
-    const int u = (int)blockIdx.x + n * (int)gridDim.x;
-    return u < units ? u : -1;
-  }
-  const int k = (int)s.start[blockIdx.x] + n;
-  return k < (int)s.start[blockIdx.x + 1] ? (int)s.unit[k] : -1;
+  pfx::unit_of(p.batch, p.heads, p.qtiles, p.group, u, b, h, qt);
 }
 
 // The CTA's control block: barriers, the row maxima exchanged between the softmax warpgroups, the unit's row sums
@@ -239,19 +101,6 @@ struct alignas(1024) Ctl {
 };
 static_assert(sizeof(Ctl) + SMEM_BYTES <= 232448, "shared memory per block");
 static_assert(NSB * 128 + D <= TMEM_COLS, "S buffers and O in TMEM");
-
-OMNI_DEV bool sync_or(int id, int count, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"((uint32_t)pred), "r"(id), "r"(count)
-      : "memory");
-  return out != 0;
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -599,26 +448,32 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int q = qt * BM + row;
       __nv_bfloat16* dst = p.out + (int64_t)b * p.out_sb + (int64_t)q * p.out_sw + (int64_t)h * p.out_sh;
+      // O in two halves of 64 columns (two loads in flight per wait), released to the next unit's first P V once the
+      // second half is in registers, before it is scaled and stored (measured: 183.0 us per config-4 call against
+      // 186.5 us with four 32-column reads and the release after the last store).
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r0[32];
-        tmem_ld32_async(tbase + lane_off + COL_O + c * 32, r0);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r0[64];
+        tmem_ld32_async(tbase + lane_off + COL_O + c * 64, r0);
+        tmem_ld32_async(tbase + lane_off + COL_O + c * 64 + 32, r0 + 32);
         tmem_wait_ld();
+        if (c == 1) {
+          tc_fence_before();
+          mbar_arrive(&o_free);
+        }
         if (q < p.width) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 8; ++i) {
             uint32_t w4[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const int k = 8 * i + 2 * j;
               w4[j] = pack_bf16x2(__uint_as_float(r0[k]) * inv, __uint_as_float(r0[k + 1]) * inv);
             }
-            *reinterpret_cast<uint4*>(dst + c * 32 + i * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            *reinterpret_cast<uint4*>(dst + c * 64 + i * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&o_free);
       if (row == 0) OMNI_TRACE_AT(1601 + nunit * 2);
     }
   }
@@ -646,60 +501,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   OMNI_TRACE_CTA(1);
 }
 
-// (row, head) pairs per scheduling group: about 16, so that one group's units cover the grid once or twice and its
-// K/V (under 13 MB at width 1500) stay in L2 while the grid works through them. OMNIASR_PREFILL_GROUP overrides.
-int prefill_group(int bh_count) {
-  static const int env = [] {
-    const char* e = getenv("OMNIASR_PREFILL_GROUP");
-    return e ? atoi(e) : 0;
-  }();
-  int g = env > 0 ? env : 16;
-  return g < bh_count ? g : bh_count;
-}
-
-// Fixed cost of a unit in key tiles (measured: a unit's first tile takes about 1.6 tiles' time).
-constexpr float kUnitCost = 0.6f;
-
-// The list schedule of `units` units (unit_of's numbering) over `grid` CTAs, cached per shape.
-const Sched* schedule(int batch, int heads, int qtiles, int group, int grid) {
-  static const bool off = [] {  // OMNIASR_PREFILL_SCHED=0: round-robin (for comparisons)
-    const char* e = getenv("OMNIASR_PREFILL_SCHED");
-    return e && atoi(e) == 0;
-  }();
-  const int units = batch * heads * qtiles;
-  if (off || units > kSchedUnits || grid > kSchedCtas) return nullptr;
-  static std::mutex mu;
-  static std::map<std::array<int, 5>, std::unique_ptr<Sched>> cache;
-  const std::array<int, 5> key{batch, heads, qtiles, group, grid};
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second.get();
-  auto s = std::make_unique<Sched>();
-  std::vector<std::vector<uint16_t>> lists(grid);
-  using Slot = std::pair<float, int>;  // (time the CTA is free, CTA)
-  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> free_at;
-  for (int c = 0; c < grid; ++c) free_at.push({0.f, c});
-  const int bh_count = batch * heads;
-  for (int u = 0; u < units; ++u) {
-    const int per_group = group * qtiles;  // unit_of's numbering, on the host
-    const int g0 = (u / per_group) * group;
-    const int gsize = std::min(group, bh_count - g0);
-    const int qt = qtiles - 1 - (u - g0 * qtiles) / gsize;
-    const Slot c = free_at.top();
-    free_at.pop();
-    lists[c.second].push_back((uint16_t)u);
-    free_at.push({c.first + (float)(qt + 1) + kUnitCost, c.second});
-  }
-  s->on = 1;
-  int k = 0;
-  for (int c = 0; c < grid; ++c) {
-    s->start[c] = (uint16_t)k;
-    for (uint16_t u : lists[c]) s->unit[k++] = u;
-  }
-  s->start[grid] = (uint16_t)k;
-  return cache.emplace(key, std::move(s)).first->second.get();
-}
-
 bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t w, int64_t sb, int64_t sh,
               int64_t sw) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
@@ -722,6 +523,69 @@ bool make_map(CUtensorMap* map, const void* base, int64_t b, int64_t h, int64_t 
 
 }  // namespace prefill
 
+// (row, head) pairs per scheduling group: about 16, so that one group's units cover the grid once or twice and its
+// K/V (under 13 MB at width 1500) stay in L2 while the grid works through them. OMNIASR_PREFILL_GROUP overrides.
+int prefill_group(int bh_count) {
+  static const int env = [] {
+    const char* e = getenv("OMNIASR_PREFILL_GROUP");
+    return e ? atoi(e) : 0;
+  }();
+  int g = env > 0 ? env : 16;
+  return g < bh_count ? g : bh_count;
+}
+
+// Fixed cost of a unit in key tiles (measured: a unit's first tile takes about 1.6 tiles' time).
+constexpr float kPrefillUnitCost = 0.6f;
+
+// The list schedule of `units` units (unit_of's numbering) over `grid` CTAs, cached per shape.
+const pfx::Sched* prefill_schedule(int batch, int heads, int qtiles, int group, int grid) {
+  static const bool off = [] {  // OMNIASR_PREFILL_SCHED=0: round-robin (for comparisons)
+    const char* e = getenv("OMNIASR_PREFILL_SCHED");
+    return e && atoi(e) == 0;
+  }();
+  const int units = batch * heads * qtiles;
+  if (off || units > pfx::kSchedUnits || grid > pfx::kSchedCtas) return nullptr;
+  static std::mutex mu;
+  static std::map<std::array<int, 5>, std::unique_ptr<pfx::Sched>> cache;
+  const std::array<int, 5> key{batch, heads, qtiles, group, grid};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second.get();
+  auto s = std::make_unique<pfx::Sched>();
+  std::vector<std::vector<uint16_t>> lists(grid);
+  using Slot = std::pair<float, int>;  // (time the CTA is free, CTA)
+  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> free_at;
+  for (int c = 0; c < grid; ++c) free_at.push({0.f, c});
+  const int bh_count = batch * heads;
+  for (int u = 0; u < units; ++u) {
+    const int per_group = group * qtiles;  // unit_of's numbering, on the host
+    const int g0 = (u / per_group) * group;
+    const int gsize = std::min(group, bh_count - g0);
+    const int qt = qtiles - 1 - (u - g0 * qtiles) / gsize;
+    const Slot c = free_at.top();
+    free_at.pop();
+    lists[c.second].push_back((uint16_t)u);
+    free_at.push({c.first + (float)(qt + 1) + kPrefillUnitCost, c.second});
+  }
+  s->on = 1;
+  int k = 0;
+  for (int c = 0; c < grid; ++c) {
+    s->start[c] = (uint16_t)k;
+    for (uint16_t u : lists[c]) s->unit[k++] = u;
+  }
+  s->start[grid] = (uint16_t)k;
+  return cache.emplace(key, std::move(s)).first->second.get();
+}
+
+const pfx::Sched& prefill_round_robin() {
+  static const pfx::Sched r = [] {
+    pfx::Sched x{};
+    x.on = 0;
+    return x;
+  }();
+  return r;
+}
+
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   using namespace prefill;
   CUtensorMap qm, km, vm;
@@ -741,7 +605,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.width = a.width;
   p.qtiles = (a.width + BM - 1) / BM;
   p.qscale = a.scale * kLog2e;
-  p.group = prefill_group(a.batch * a.heads);
+  p.group = omni::prefill_group(a.batch * a.heads);
   p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
   p.q_sb = a.q_sb;
   p.q_sh = a.q_sh;
@@ -755,14 +619,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   int grid = device_sm_count();
   if (grid > units) grid = units;
   if (grid <= 0) return cudaSuccess;
-  static const Sched round_robin = [] {
-    Sched r{};
-    r.on = 0;
-    return r;
-  }();
-  const Sched* sched = schedule(p.batch, p.heads, p.qtiles, p.group, grid);
+  const Sched* sched = prefill_schedule(p.batch, p.heads, p.qtiles, p.group, grid);
   return launch_dependent(prefill_kernel, dim3(grid), dim3(THREADS), (size_t)SMEM_BYTES, stream, qm, km, vm, p,
-                          sched ? *sched : round_robin);
+                          sched ? *sched : prefill_round_robin());
 }
 
 }  // namespace omni

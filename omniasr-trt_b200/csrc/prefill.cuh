@@ -23,5 +23,7 @@ struct PrefillArgs {
 };
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+// The same for head_dim 512 (prefill_wide.cu): tensors [batch, heads, width, 512].
+cudaError_t launch_prefill_wide(const PrefillArgs& a, cudaStream_t stream);
 
 }  // namespace omni

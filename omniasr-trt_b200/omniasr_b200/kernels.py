@@ -243,9 +243,9 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
     """Causal attention of prefilled contexts: ``q``/``k``/``v`` [B, H, W, D] (any strides, unit stride in D; k and
     v typically cache views); query w sees keys [0, w]. Returns [B, H, W, D] in q's dtype -- a view of a
     [B, W, H, D] buffer, so the caller's ``o.transpose(1, 2).reshape(B * W, -1)`` costs nothing. This is the
-    reference's ``F.scaled_dot_product_attention(q, k, v, is_causal=True)`` (decode.py:171): bf16 head_dim 128 runs
-    on the tensor-core prefill kernel, bf16 head_dim 512 on the tensor-core decode pass in groups of 16 query
-    positions; other dtypes / head dims run as a drafted verify with W queries per row on the CUDA cores."""
+    reference's ``F.scaled_dot_product_attention(q, k, v, is_causal=True)`` (decode.py:171): bf16 head_dim 128 and
+    512 run on the tensor-core prefill kernels; other dtypes / head dims run as a drafted verify with W queries per
+    row on the CUDA cores. :func:`prefill_attention_grouped` is the head_dim-512 alternative on the decode pass."""
     b, heads, width, dim = q.shape
     scale = dim**-0.5 if scale is None else float(scale)
     out = torch.empty(b, width, heads, dim, dtype=q.dtype, device=q.device)
@@ -253,9 +253,7 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
         return out.transpose(1, 2)
     if k.shape != q.shape or v.shape != q.shape or q.stride(3) != 1 or k.stride(3) != 1 or v.stride(3) != 1:
         raise ValueError("prefill_attention: q, k, v must be [B, H, W, D] with unit stride in D")
-    if q.dtype == torch.bfloat16 and dim == 512:
-        return _prefill_grouped(q, k, v, scale)
-    if q.dtype == torch.bfloat16 and dim == 128:
+    if q.dtype == torch.bfloat16 and dim in (128, 512):
         _lib.call("omniasr_prefill_attention", _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k), k.stride(0),
                   k.stride(1), k.stride(2), _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(out), out.stride(0),
                   out.stride(2), out.stride(1), b, heads, width, dim, scale, _lib.BF16,
@@ -273,11 +271,17 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: 
 _PREFILL_GROUP = 16  # query positions per group of the grouped prefill
 
 
-def _prefill_grouped(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+def prefill_attention_grouped(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                              scale: float | None = None) -> torch.Tensor:
     """bf16 head_dim 512: every row's queries as groups of 16 consecutive positions on the tensor-core decode pass
     (omniasr_prefill_attention_grouped), the queries padded to a multiple of 16 positions; rows are split into calls
-    of at most 16384 (group, head) units."""
+    of at most 16384 (group, head) units. The same result as :func:`prefill_attention` (within bf16 rounding)."""
     b, heads, width, dim = q.shape
+    if q.dtype != torch.bfloat16 or dim != 512 or q.stride(3) != 1 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("prefill_attention_grouped: bf16 [B, H, W, 512] q, k, v with unit stride in D")
+    scale = dim**-0.5 if scale is None else float(scale)
+    if b == 0 or width == 0:
+        return torch.empty(b, width, heads, dim, dtype=q.dtype, device=q.device).transpose(1, 2)
     wp = -(-width // _PREFILL_GROUP) * _PREFILL_GROUP
     if k.stride() != v.stride() or k.stride(3) != 1:
         k, v = k.contiguous(), v.contiguous()

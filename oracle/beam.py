@@ -6,9 +6,9 @@ groups of ``beams`` rows:
 * candidates (beam.py:161-170): ``score + logp``, or with length normalisation when the group's row 0 has counted
   tokens ``(score * count + logp) / (count + 1)``, every operation rounded to float32 as torch's elementwise
   kernels round it; an ended row offers only EOS, at its score (everything else -inf);
-* the group's best ``beams`` of its beams x vocab candidates (beam.py:171), ordered as ``torch.topk(sorted=True)``
-  on a CUDA tensor orders them: value descending, equal values by flat index ascending (torch.topk on the CPU
-  breaks ties in no fixed order, so golden vectors made on the CPU avoid ties at the selection);
+* the group's best ``beams`` of its beams x vocab candidates (beam.py:171), in the order ``torch.topk(sorted=True)``
+  returns them for a CUDA tensor (:func:`topk_order`; torch.topk on the CPU orders ties in no fixed way, so golden
+  vectors made on the CPU avoid ties at the selection);
 * parents, new tokens and the rows' reorder (beam.py:172-187).
 
 Arrays are numpy and are updated in place: ``logp`` [R, V] float32 (bf16 values widened), ``score`` [R] float32,
@@ -21,13 +21,54 @@ from __future__ import annotations
 import numpy as np
 
 
-def topk_order(values: np.ndarray, k: int) -> np.ndarray:
-    """Indices of the ``k`` largest values, value descending and index ascending among equal values."""
+def _order_key(values: np.ndarray) -> np.ndarray:
+    """Float32 values as order-preserving integers (int64): -0 counts as +0, NaN as larger than +inf."""
     v = values.astype(np.float32)
-    v = np.where(v == 0, np.float32(0), v)  # -0 and +0 compare equal
-    v = np.where(np.isnan(v), np.float32(np.inf), v)
-    nan_first = np.isnan(values)  # NaN counts as larger than +inf
-    return np.lexsort((np.arange(v.size), -v, ~nan_first))[:k]
+    v = np.where(v == 0, np.float32(0), v).astype(np.float32)
+    b = v.view(np.uint32).astype(np.int64)
+    b = np.where(np.isnan(v), 0x7FC00000, b)
+    return np.where(b & 0x80000000, (~b) & 0xFFFFFFFF, b | 0x80000000)
+
+
+def topk_order(values: np.ndarray, k: int) -> np.ndarray:
+    """Indices of the ``k`` <= 32 largest values in the order ``torch.topk(sorted=True)`` returns them for a CUDA
+    tensor (pinned by tests/golden/topk_ties.npz, made with torch on a GPU): the values above the k-th largest, then
+    those equal to it, each in index order; then a bitonic sorting network over 32 slots (unused slots last) whose
+    compare-exchange keeps a pair only when the first entry is the larger, so equal values move with their slots."""
+    key = _order_key(values)
+    order = np.lexsort((np.arange(key.size), -key))
+    kth = key[order[k - 1]]
+    above = np.sort(order[:k][key[order[:k]] > kth])
+    equal = np.nonzero(key == kth)[0][: k - above.size]
+    pre = list(above) + list(equal)
+    size_p = 32
+    kv = [int(key[i]) for i in pre] + [0] * (size_p - k)
+    ix = pre + [-1] * (size_p - k)
+    ok = [True] * k + [False] * (size_p - k)
+
+    def exchange(a: int, b: int, direction: bool):
+        s = (kv[a] > kv[b] and ok[a]) or not ok[b]
+        if s == direction:
+            kv[a], kv[b] = kv[b], kv[a]
+            ix[a], ix[b] = ix[b], ix[a]
+            ok[a], ok[b] = ok[b], ok[a]
+
+    size = 2
+    while size < size_p:
+        stride = size // 2
+        while stride:
+            for t in range(size_p // 2):
+                pos = 2 * t - (t & (stride - 1))
+                exchange(pos, pos + stride, (t & (size // 2)) != 0)
+            stride //= 2
+        size *= 2
+    stride = size_p // 2
+    while stride:
+        for t in range(size_p // 2):
+            pos = 2 * t - (t & (stride - 1))
+            exchange(pos, pos + stride, False)
+        stride //= 2
+    return np.array(ix[:k], dtype=np.int64)
 
 
 def candidates(logp: np.ndarray, score: np.ndarray, ended: np.ndarray, count: np.ndarray, beams: int,

@@ -89,22 +89,23 @@ def test_beam_d512_config3_shape(K, beams):
     assert K.read_status() == 0
 
 
+@pytest.mark.parametrize("path", ["wide", "grouped"])
 @pytest.mark.parametrize("b,w", [(2, 70), (3, 129), (8, 1500)])
-def test_prefill_d512_grouped(K, b, w):
-    """The causal prefill at 8 x 512 runs on the tensor-core pass in groups of 16 query positions (ragged last
-    group, cache views longer than the width). Checked on every (row, head) at sampled positions; config 4's 8 x 1500
-    among the shapes."""
+def test_prefill_d512(K, b, w, path):
+    """The causal prefill at 8 x 512: the two-pass tensor-core prefill kernel (prefill_attention) and the decode pass
+    in groups of 16 query positions (prefill_attention_grouped); ragged last tiles and groups, cache views longer
+    than the width. Checked on every (row, head) at sampled positions; config 4's 8 x 1500 among the shapes."""
     cap = w + 37
     q = randn((b * w, H, D), torch.bfloat16, 530 + w).cuda().view(b, w, H, D).transpose(1, 2)
     kc = randn((b + 1, H, cap, D), torch.bfloat16, 531 + w).cuda()
     vc = randn((b + 1, H, cap, D), torch.bfloat16, 532 + w).cuda()
     k, v = kc[:b, :, :w], vc[:b, :, :w]
-    out = K.prefill_attention(q, k, v)
+    out = (K.prefill_attention if path == "wide" else K.prefill_attention_grouped)(q, k, v)
     assert out.shape == (b, H, w, D)
     g = torch.Generator().manual_seed(533)
     pos = torch.cat([torch.tensor([0, 15, 16, w - 1]), torch.randint(0, w, (28,), generator=g)]).clamp(max=w - 1).unique()
     qc, kcc, vcc, oc = q.cpu(), k.cpu(), v.cpu(), out.cpu()
     for hh in range(H):
         want = oatt.prefill_attention_rows(qc[:, hh:hh + 1], kcc[:, hh:hh + 1], vcc[:, hh:hh + 1], pos)
-        check_attention(oc[:, hh:hh + 1, pos], want, torch.bfloat16, what=f"prefill 8x512 b={b} w={w} head {hh}")
+        check_attention(oc[:, hh:hh + 1, pos], want, torch.bfloat16, what=f"prefill 8x512 {path} b={b} w={w} h{hh}")
     assert K.read_status() == 0

@@ -211,9 +211,15 @@ def test_beam_select_oracle_matches_reference_golden():
 
 
 def test_beam_select_oracle_tie_order():
-    """Equal candidates order by flat index (value descending first), as torch.topk orders them on a CUDA tensor."""
+    """Equal values in the order torch.topk(sorted=True) returns them on a CUDA tensor, which is how the reference's
+    beam search selects (beam.py:171): recorded with torch on a GPU (tests/golden/make_topk_golden.py)."""
     from oracle import beam
 
-    v = np.array([1.0, 3.0, 3.0, 2.0, 3.0, -0.0, 0.0, 3.0], dtype=np.float32)
-    assert beam.topk_order(v, 5).tolist() == [1, 2, 4, 7, 3]
-    assert beam.topk_order(np.array([0.0, -0.0, 0.0], dtype=np.float32), 3).tolist() == [0, 1, 2]
+    z = np.load(GOLDEN / "topk_ties.npz")
+    for k in range(1, 33):
+        assert np.array_equal(beam.topk_order(np.zeros(40, np.float32), k), z[f"eq_k{k}"]), k
+    for i in range(int(z["n"])):
+        codes = z[f"case{i}_x"]
+        x = np.where(codes < 0, -np.inf, codes).astype(np.float32)
+        want = z[f"case{i}_i"]
+        assert np.array_equal(beam.topk_order(x, len(want)), want), i

@@ -2,9 +2,9 @@
 heads, vocab 10288), once with these kernels dropped in and once with the reference's own Triton kernels, on the same
 seeded weights and prefix embeddings. In fp32 the two must give the same tokens at every position. In bf16 a
 random-weight model's logits lie close together and rounding differences may flip an argmax, so the bf16 test reports,
-per row, the first position where the two token sequences differ and the top-2 logit margin there (from a
-teacher-forced bf16 forward of the reference's tokens through the reference's own ``decoder_forward``), and requires
-both tokens to be that forward's two best. Each arm runs ``bench.py --workload step`` in its own process, since the
+per row, the first position where the two token sequences differ, the two tokens' logits and the top-2 logit margin
+there (from a teacher-forced bf16 forward of the reference's tokens through the reference's own ``decoder_forward``),
+and requires both tokens' logits to lie within a few bf16 steps of each other and of the best one. Each arm runs ``bench.py --workload step`` in its own process, since the
 drop-in replaces the reference's kernel module for the whole process."""
 
 import subprocess
@@ -76,7 +76,7 @@ def _teacher_forced_top2(tokens: np.ndarray, first_div: list[int]) -> list[dict]
             logits = m.final_proj(h[0, -1]).float()
             top = logits.topk(2)
             out.append({"logits": top.values.tolist(), "tokens": top.indices.tolist(),
-                        "margin": float(top.values[0] - top.values[1])})
+                        "margin": float(top.values[0] - top.values[1]), "all": logits.cpu()})
     del m
     torch.cuda.empty_cache()
     return out
@@ -104,11 +104,15 @@ def test_full_decoder_bf16_first_divergence_report(tmp_path):
             lines.append(f"row {r}: identical over {min(generated(a[r]), generated(b[r]))} tokens")
             continue
         t = top2[r]
+        la, lb = float(t["all"][int(a[r, d])]), float(t["all"][int(b[r, d])])
         lines.append(f"row {r}: first divergence at generated token {d} (ours {int(a[r, d])}, reference "
-                     f"{int(b[r, d])}); teacher-forced bf16 top-2 {t['tokens']} logits "
-                     f"{[round(v, 4) for v in t['logits']]}, margin {t['margin']:.4f}")
-        # A rounding flip: both kernel sets chose among the two best candidates of the reference's own forward.
-        assert {int(a[r, d]), int(b[r, d])} <= set(t["tokens"]), lines[-1]
+                     f"{int(b[r, d])}); teacher-forced bf16 logits of the two {la:.4f} / {lb:.4f}, top-2 "
+                     f"{t['tokens']} {[round(v, 4) for v in t['logits']]}, top-2 margin {t['margin']:.4f}")
+        # A rounding flip: the two tokens' logits in the reference's own forward lie within a few bf16 steps of each
+        # other and of the best logit (a bf16 step at magnitude x is 2^(floor(log2 x) - 7); the decoders' logits come
+        # from drafted verify steps, this forward from one causal pass, so they differ by rounding too).
+        step = 2.0 ** (np.floor(np.log2(max(abs(la), abs(lb), abs(t["logits"][0]), 1e-3))) - 7)
+        assert abs(la - lb) <= 8 * step and t["logits"][0] - min(la, lb) <= 8 * step, lines[-1]
     report = "\n".join(lines)
     print("bf16 first-divergence report (config 4, SpecDecoder, 32 steps):\n" + report)
     (ROOT / "gpurun_out").mkdir(exist_ok=True)
