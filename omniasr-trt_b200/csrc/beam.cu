@@ -79,53 +79,46 @@ OMNI_DEV void warp_merge(uint64_t (&best)[NB], uint64_t* out) {
 // beams x vocab candidates), on the k keys `best` holds in (value descending, index ascending) order: its selection
 // lists the values above the k-th best value, then those equal to it, each in index order, and its sort of those k is
 // a bitonic network over 32 slots (the unused slots last) that exchanges two entries unless the first is the larger,
-// so equal values end up in an order fixed by their slots. One thread; the network's stages in sequence.
-__device__ __noinline__ void torch_order(uint64_t* best, int n) {
-  constexpr int P = 32;
-  uint32_t kv[P], ix[P];
-  bool ok[P];
+// so equal values end up in an order fixed by their slots. One warp, lane = slot; `pre` is 32 words of scratch.
+OMNI_DEV void torch_order(uint64_t* best, int n, uint64_t* pre) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t mine = lane < n ? best[lane] : 0;
   const uint32_t kth = (uint32_t)(best[n - 1] >> 32);
-  int m = 0;
-  for (int pass = 0; pass < 2; ++pass) {  // above the k-th value, then equal to it; each by index
-    const int first = m;
-    for (int j = 0; j < n; ++j) {
-      const uint32_t hi = (uint32_t)(best[j] >> 32);
-      if (pass == 0 ? hi <= kth : hi != kth) continue;
-      kv[m] = hi;
-      ix[m] = key_index(best[j]);
-      int i = m++;
-      while (i > first && ix[i - 1] > ix[i]) {  // insertion by index
-        const uint32_t tk = kv[i], ti = ix[i];
-        kv[i] = kv[i - 1];
-        ix[i] = ix[i - 1];
-        kv[i - 1] = tk;
-        ix[i - 1] = ti;
-        --i;
-      }
-    }
+  const bool above = lane < n && (uint32_t)(mine >> 32) > kth;
+  const int n_above = __popc(__ballot_sync(0xffffffffu, above));
+  int rank = above ? 0 : n_above;  // the place in the selection's list: its class, then index order within it
+  for (int i = 0; i < n; ++i) {
+    const uint64_t other = __shfl_sync(0xffffffffu, mine, i);
+    const bool other_above = (uint32_t)(other >> 32) > kth;
+    if (lane < n && other_above == above && key_index(other) < key_index(mine)) ++rank;
   }
-  for (int i = 0; i < P; ++i) ok[i] = i < n;
-  for (int i = n; i < P; ++i) kv[i] = ix[i] = 0;
-  auto exchange = [&](int x, int y, bool dir) {
-    const bool s = (kv[x] > kv[y] && ok[x]) || !ok[y];
+  if (lane < n) pre[rank] = mine;
+  __syncwarp();
+  uint32_t kv = lane < n ? (uint32_t)(pre[lane] >> 32) : 0u;
+  uint32_t ix = lane < n ? key_index(pre[lane]) : 0u;
+  bool ok = lane < n;
+  // One compare-exchange stage: slot `lane` and slot `lane ^ stride`; the lower of the two is the network's first
+  // entry, its direction bit `size` of its position (the final merge: always 0).
+  auto stage = [&](int size, int stride, bool merge) {
+    const uint32_t pk = __shfl_xor_sync(0xffffffffu, kv, stride);
+    const uint32_t pi = __shfl_xor_sync(0xffffffffu, ix, stride);
+    const bool pv = __shfl_xor_sync(0xffffffffu, ok, stride);
+    const bool lower = (lane & stride) == 0;
+    const uint32_t ka = lower ? kv : pk, kb = lower ? pk : kv;
+    const bool va = lower ? ok : pv, vb = lower ? pv : ok;
+    const bool dir = merge ? false : ((lane & ~stride) & size) != 0;
+    const bool s = (ka > kb && va) || !vb;
     if (s == dir) {
-      const uint32_t tk = kv[x], ti = ix[x];
-      const bool tv = ok[x];
-      kv[x] = kv[y];
-      ix[x] = ix[y];
-      ok[x] = ok[y];
-      kv[y] = tk;
-      ix[y] = ti;
-      ok[y] = tv;
+      kv = pk;
+      ix = pi;
+      ok = pv;
     }
   };
-  for (int size = 2; size < P; size *= 2)
-    for (int stride = size / 2; stride > 0; stride /= 2)
-      for (int t = 0; t < P / 2; ++t) exchange(2 * t - (t & (stride - 1)), 2 * t - (t & (stride - 1)) + stride,
-                                               (t & (size / 2)) != 0);
-  for (int stride = P / 2; stride > 0; stride /= 2)
-    for (int t = 0; t < P / 2; ++t) exchange(2 * t - (t & (stride - 1)), 2 * t - (t & (stride - 1)) + stride, false);
-  for (int j = 0; j < n; ++j) best[j] = ((uint64_t)kv[j] << 32) | (uint32_t)~ix[j];
+  for (int size = 2; size < 32; size *= 2)
+    for (int stride = size / 2; stride > 0; stride /= 2) stage(size, stride, false);
+  for (int stride = 16; stride > 0; stride /= 2) stage(32, stride, true);
+  if (lane < n) best[lane] = ((uint64_t)kv << 32) | (uint32_t)~ix;
+  __syncwarp();
 }
 
 struct Row {
@@ -222,7 +215,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads) bea
   }
   cluster.sync();  // the lists have been read: a CTA may leave once it is done
 
-  if (live && tid == 0) torch_order(group_best, n);
+  if (live && warp == 0) torch_order(group_best, n, warp_best[0]);  // warp_best is free again
   __syncthreads();
 
   // -------------------------------------------------------------------- parents, new tokens (beam.py:172-178)
