@@ -602,7 +602,7 @@ class Gemm(Workload):
         return [last] if i == self.layers - 1 else []
 
     def run_library(self):
-        """The same GEMMs as the reference computes them (torch / cuBLAS)."""
+        """torch.matmul / addmm (cuBLAS) and the SwiGLU elementwise, as the reference's decoder step computes them."""
         outs = []
         for i in range(self.layers):
             qkv_w, out_w, gi_w, ffo_w = self.w[i]
@@ -629,6 +629,73 @@ class Gemm(Workload):
             return 2 * cls.D_MODEL * cls.D_MODEL
 
         return one, "the output projection (4096 x 4096, 40 rows) in torch on the CPU"
+
+
+class QkvRope(Workload):
+    """Row f1: the decoder step's QKV product with RoPE and the KV-cache append in its epilogue
+    (kernels.decode_gemm_rope), for config 2's 8 rows x 5 tokens, 12 layers of distinct weights."""
+
+    name = "qkvrope"
+    roof_timing = "whole"
+    metric = "QKV + RoPE/append weight-streaming GB/s (40 tokens, 4096 -> 3 x 32 x 128, 12 layers)"
+    roof_kernel = "decode_gemm_rope (12288 x 4096, RoPE + cache append in the epilogue)"
+    traffic_key = "decode_gemm_rope_bytes_per_call"
+    B, T, D_MODEL, CAP = 8, 5, 4096, 4096
+
+    def __init__(self, *a):
+        super().__init__(*a)
+        n, Dm = self.B * self.T, self.D_MODEL
+        w = lambda r, c: (torch.randn(r, c, generator=self.gen, device=self.device) * 0.02).to(torch.bfloat16)  # noqa
+        self.w = [w(3 * Dm, Dm) for _ in range(self.layers)]
+        self.x = self.randn(n, Dm)
+        from oracle import rope as orope
+
+        self.cs = orope.rope_table(D, self.CAP + 8).contiguous().to(self.device)
+        g = cpu_gen(0)
+        base = torch.randint(200, 2001, (self.B,), generator=g)
+        self.pos = (base[:, None] + torch.arange(self.T)[None]).reshape(-1).to(self.device)
+        self.slots = torch.arange(self.B).repeat_interleave(self.T).to(self.device)
+        self.kc = self.randn(self.B, H, self.CAP, D)
+        self.vc = self.randn(self.B, H, self.CAP, D)
+        self.roof_units = 2 * 3 * Dm * Dm + n * Dm * 2 + 3 * n * H * D * 2  # weights, x, q + k + v written
+        self.step_units = self.roof_units * self.layers
+
+    def layer_in(self, i):
+        return [self.x] if i == 0 else []
+
+    def layer(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        q = self.K.decode_gemm_rope(self.x, self.w[i], self.cs, self.pos, self.kc, self.vc, H, slots=self.slots)
+        if ev:
+            ev[1].record()
+        return [q] if i == self.layers - 1 else []
+
+    def run_library(self):
+        """The reference's sequence: the product by torch (cuBLAS), then RoPE + append (this library's rope_kv)."""
+        outs = []
+        for i in range(self.layers):
+            qkv = self.x @ self.w[i].t()
+            outs.append(self.K.rope_kv(qkv, self.cs, self.pos, self.kc, self.vc, H, slots=self.slots))
+        return outs
+
+    def config(self):
+        return {"workload": "row f1: QKV product + RoPE + KV append for config 2's 40 tokens (8 rows x spec-4 + 1), "
+                            "32 x 128 heads, d_model 4096, 12 layers of distinct weights (1.2 GB per step)",
+                "rows": self.B * self.T, "layers": self.layers, "bytes_per_step_per_gpu": self.step_units,
+                "l2": "inputs larger than L2 (12 distinct 100 MB weight matrices per step)"}
+
+    @classmethod
+    def cpu_sampler(cls):
+        g = cpu_gen(0)
+        x = torch.randn(cls.B * cls.T, cls.D_MODEL, generator=g).to(torch.bfloat16)
+        w = (torch.randn(3 * cls.D_MODEL, cls.D_MODEL, generator=g) * 0.02).to(torch.bfloat16)
+
+        def one():
+            x @ w.t()
+            return 2 * 3 * cls.D_MODEL * cls.D_MODEL
+
+        return one, "the QKV product (12288 x 4096, 40 rows) in torch on the CPU (RoPE left out)"
 
 
 class Select(Workload):
@@ -711,7 +778,7 @@ class Select(Workload):
         return one, "one selection step of the 8 x 5 beams (numpy oracle, fp32 log-probabilities)"
 
 
-WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm, Select)}
+WORKLOADS = {w.name: w for w in (Verify, Decode, Beam, Gather, Prefill, Sweep, Gemm, Select, QkvRope)}
 
 
 # ------------------------------------------------------------------------------- the reference's own GPU kernels
@@ -1096,8 +1163,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         torch.cuda.synchronize(device)
         lib_ms = s3.elapsed_time(e3) / args.steps
         line["library_baseline"] = {"value": round(wl.step_units / (lib_ms * 1e-3) / scale, 1), "unit": wl.unit,
-                                    "ms_per_step": round(lib_ms, 4), "what": "torch.matmul / addmm (cuBLAS) and "
-                                    "the SwiGLU elementwise, as the reference's decoder step computes them"}
+                                    "ms_per_step": round(lib_ms, 4),
+                                    "what": (wl.run_library.__doc__ or "").strip().replace("\n", " ")
+                                    or "the same work through torch / cuBLAS"}
     if world == 1 and args.cpu_seconds > 0:
         line["cpu_baseline"] = cpu_time(WORKLOADS[args.workload], args.cpu_seconds)
     return line

@@ -212,6 +212,20 @@ int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w
                         int mode, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
                         void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
 
+/* The QKV product of the decoder step with RoPE and the KV-cache append in its epilogue (bf16, rows <= 64): the
+ * product qkv = x . w^T (w [3 * heads * dim, k]) is formed, each value rounded to bf16 as the GEMM's output would
+ * be, and then handled as omniasr_rope_kv() handles a qkv row -- q rotated into q_out [rows, heads, dim], k rotated
+ * and v as it is written into the caches at cache row slots[m] (or m) and position cache_pos[m] (or pos[m]) -- without
+ * qkv ever reaching memory. Arguments as omniasr_decode_gemm() and omniasr_rope_kv(); the workspace is sized by
+ * omniasr_decode_gemm_workspace(rows, 3 * heads * dim, k, OMNIASR_GEMM_STORE) and follows the same counter rule.
+ * dim must be a multiple of 128. Replaces `qkv = norm(h) @ qkv_w.t()` followed by kernels.rope_kv
+ * (omniasr_trt/decode.py:201-203, spec.py:100-101). */
+int omniasr_decode_gemm_rope(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int k,
+                             const float* cs, int64_t cs_positions, const int64_t* pos, const int64_t* slots,
+                             const int64_t* cache_pos, void* q_out, void* k_cache, void* v_cache, int64_t cache_rows,
+                             int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos, int heads,
+                             int dim, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream);
+
 /* Flash-decode for callers that cannot allocate device memory (no counterpart in the reference, whose
  * wrappers allocate their partials with torch.empty): the same computation and arguments as
  * omniasr_decode_attention() minus the workspace, which here is a device array inside this library of

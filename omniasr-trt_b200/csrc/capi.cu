@@ -678,6 +678,57 @@ size_t omniasr_decode_gemm_workspace(int rows, int n, int k, int mode) {
   return omni::gemm_workspace_bytes(rows, n, k, mode);
 }
 
+int omniasr_decode_gemm_rope(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int k,
+                             const float* cs, int64_t cs_positions, const int64_t* pos, const int64_t* slots,
+                             const int64_t* cache_pos, void* q_out, void* k_cache, void* v_cache, int64_t cache_rows,
+                             int64_t cache_len, int64_t stride_row, int64_t stride_head, int64_t stride_pos, int heads,
+                             int dim, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+  if (int e = check_device()) return e;
+  if (rows < 0 || rows > omni::kGemmMaxRows || k < 0 || heads <= 0 || dim <= 0 || dim % 128 != 0)
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm_rope: rows %d (at most %d), k %d, heads %d, dim %d (a multiple of "
+                "128)", rows, omni::kGemmMaxRows, k, heads, dim);
+  if (rows == 0) return ok();
+  if (k == 0) return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm_rope: k = 0");
+  if (!x || !w || !workspace || !cs || !pos || !q_out) return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm_rope: null pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(workspace) || !aligned16(cs) || (x_stride * 2) % 16 ||
+      (w_stride * 2) % 16 || x_stride < k || w_stride < k)
+    return fail(OMNIASR_ERR_ARGUMENT, "decode_gemm_rope: x / w / cs must be 16-byte aligned, row strides >= k");
+  if (int e = check_cache("decode_gemm_rope", k_cache, v_cache, cache_rows, cache_len, stride_row, stride_head,
+                          stride_pos, heads, dim, OMNIASR_BF16))
+    return e;
+  const int n = 3 * heads * dim;
+  if (omni::gemm_tiles(n, omni::kGemmStore) > omni::kGemmMaxTiles)
+    return fail(OMNIASR_ERR_UNSUPPORTED, "decode_gemm_rope: n %d needs more than %d weight tiles", n,
+                omni::kGemmMaxTiles);
+  const size_t need = omni::gemm_workspace_bytes(rows, n, k, omni::kGemmStore);
+  if (workspace_bytes < need)
+    return fail(OMNIASR_ERR_WORKSPACE, "decode_gemm_rope: workspace %zu bytes, %zu needed", workspace_bytes, need);
+  omni::GemmArgs a{};
+  a.rows = rows;
+  a.n = n;
+  a.k = k;
+  a.mode = omni::kGemmRope;
+  a.status = status;
+  a.head_dim = dim;
+  a.rope.cs = cs;
+  a.rope.cs_positions = cs_positions;
+  a.rope.pos = pos;
+  a.rope.slots = slots;
+  a.rope.cache_pos = cache_pos;
+  a.rope.q_out = q_out;
+  a.rope.k_cache = k_cache;
+  a.rope.v_cache = v_cache;
+  a.rope.s_kb = stride_row;
+  a.rope.s_kh = stride_head;
+  a.rope.s_ks = stride_pos;
+  a.rope.cache_rows = cache_rows;
+  a.rope.cache_len = cache_len;
+  a.rope.heads = heads;
+  a.rope.status = status;
+  return cuda_status(omni::launch_decode_gemm(x, x_stride, w, w_stride, a, workspace, workspace_bytes, stream),
+                     "decode_gemm_rope launch");
+}
+
 int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int n, int k,
                         int mode, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
                         void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {

@@ -55,6 +55,26 @@ struct Layout {
 
 OMNI_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// kGemmRope: a token's place, staged in shared memory once per CTA by the epilogue threads (thread m = token m):
+// the offset of its cos/sin row (-1: position outside the table) and of its cache slot (-1: outside the cache).
+struct TokenPlace {
+  int64_t cs_off;
+  int64_t cache_off;
+};
+
+OMNI_DEV void stage_tokens(const GemmArgs& a, int m, TokenPlace* place) {
+  if (m >= a.rows) return;
+  const RopeArgs& r = a.rope;
+  const int64_t p = r.pos[m];
+  const int64_t crow = r.slots ? r.slots[m] : m;
+  const int64_t cp = r.cache_pos ? r.cache_pos[m] : p;
+  const bool pos_ok = p >= 0 && p < r.cs_positions;
+  const bool dst_ok = crow >= 0 && crow < r.cache_rows && cp >= 0 && cp < r.cache_len;
+  if (!pos_ok || !dst_ok) raise_status(a.status, kStatusIndex);
+  place[m].cs_off = pos_ok ? p * a.head_dim : -1;
+  place[m].cache_off = dst_ok ? crow * r.s_kb + cp * r.s_ks : -1;
+}
+
 // The epilogue of one finished weight tile: thread `row` (0..127) holds acc[m] of token m for weight row
 // tile * 128 + row (SwiGLU: rows 0..63 gate, 64..127 inner of outputs tile * 64 + row % 64). `xch` is shared memory
 // of the 128 participating threads, which all call this together (named barrier `bar`).
@@ -81,6 +101,58 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
       }
     }
     named_sync(bar, 128);  // xch free again
+    return;
+  }
+  if (MODE == kGemmRope) {
+    // Feature f = tile * 128 + row is head dim d of head h of section q / k / v (128 divides the head_dim, so a
+    // rotation pair (2j, 2j + 1) never straddles two tiles: its partner is the neighbouring lane). Each product is
+    // rounded to bf16 first, as the GEMM's output would be, then rotated in fp32 with the non-contracting products
+    // of rope_kv.cu (omniasr_trt/modeling.py:301-306). The tokens' places come from shared memory (`xch`, staged by
+    // stage_tokens); their cos/sin pairs are fetched eight tokens at a time ahead of the stores.
+    const RopeArgs& r = a.rope;
+    const TokenPlace* place = reinterpret_cast<const TokenPlace*>(xch);
+    const int f = tile * BM + row;
+    const int per = r.heads * a.head_dim;
+    const int part = f / per, h = (f - part * per) / a.head_dim, d = f - part * per - h * a.head_dim;
+    const bool odd = d & 1;
+    const float* cs_base = r.cs + (d & ~1);
+    __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(r.q_out) + (int64_t)h * a.head_dim + d;
+    const int64_t head_off = (int64_t)h * r.s_kh + d;
+#pragma unroll
+    for (int m0 = 0; m0 < NT; m0 += 8) {
+      float2 cs[8];
+      int64_t coff[8];
+      bool rot[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = m0 + j;
+        const int64_t so = m < a.rows && part < 2 ? place[m].cs_off : -1;
+        coff[j] = m < a.rows ? place[m].cache_off : -1;
+        rot[j] = so >= 0;
+        cs[j] = rot[j] ? __ldg(reinterpret_cast<const float2*>(cs_base + so)) : make_float2(0.f, 0.f);
+        if (so < 0) coff[j] = part < 2 ? -1 : coff[j];  // no k without a rotation (v needs none)
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = m0 + j;
+        const float x = bf16r(acc[m]);
+        const float other = __shfl_xor_sync(0xffffffffu, x, 1);
+        if (m >= a.rows || f >= a.n) continue;
+        if (part == 2) {
+          if (coff[j] >= 0) reinterpret_cast<__nv_bfloat16*>(r.v_cache)[coff[j] + head_off] = __float2bfloat16_rn(x);
+          continue;
+        }
+        const float re = odd ? other : x, im = odd ? x : other;
+        const float y = !rot[j] ? 0.f
+                        : odd   ? __fadd_rn(__fmul_rn(re, cs[j].y), __fmul_rn(im, cs[j].x))
+                                : __fsub_rn(__fmul_rn(re, cs[j].x), __fmul_rn(im, cs[j].y));
+        if (part == 0) {
+          q_out[(int64_t)m * r.heads * a.head_dim] = __float2bfloat16_rn(y);  // zero for a position outside the table
+        } else if (coff[j] >= 0) {
+          reinterpret_cast<__nv_bfloat16*>(r.k_cache)[coff[j] + head_off] = __float2bfloat16_rn(y);
+        }
+      }
+    }
     return;
   }
   const int n = tile * BM + row;
@@ -219,6 +291,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
+    if (MODE == kGemmRope) {  // the tokens' places, once per CTA (the exchange area is free in this mode)
+      if (row < kGemmMaxRows) stage_tokens(a, row, reinterpret_cast<TokenPlace*>(xch));
+      named_sync(3, 128);
+    }
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
       const int t = (int)(u / a.chunks), c0 = (int)(u % a.chunks);
@@ -336,6 +412,8 @@ cudaError_t launch_mode(const CUtensorMap& wm, const CUtensorMap& xm, const Gemm
       return launch_t<NT, kGemmResidual>(wm, xm, a, stream);
     case kGemmSwiglu:
       return launch_t<NT, kGemmSwiglu>(wm, xm, a, stream);
+    case kGemmRope:
+      return launch_t<NT, kGemmRope>(wm, xm, a, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "rope_kv.cuh"
+
 namespace omni {
 
 // Decode GEMM (wgemm.cu): y = epilogue(x . w^T) for at most 64 token rows, bf16 in, fp32 accumulate, bf16 out.
@@ -12,6 +14,7 @@ enum GemmMode : int {
   kGemmStore = 0,     // y[m, n] = acc
   kGemmResidual = 1,  // y[m, n] = residual[m, n] + acc                       (torch.addmm(residual, x, w.t()))
   kGemmSwiglu = 2,    // w = [gate (n rows); inner (n rows)]: y[m, f] = inner * silu(gate), each rounded to bf16 first
+  kGemmRope = 3,      // the QKV product, then RoPE + KV-cache append as rope_kv does it (no qkv is stored): rope.*
 };
 
 struct GemmArgs {
@@ -26,6 +29,8 @@ struct GemmArgs {
   int tiles, chunks, grid;
   int64_t per;  // (tile, chunk) units per CTA
   int* status;
+  RopeArgs rope;  // kGemmRope: positions, cos/sin table, q output, caches (rope.qkv unused)
+  int head_dim;   // kGemmRope: n = 3 * rope.heads * head_dim
 };
 
 constexpr int kGemmMaxRows = 64;

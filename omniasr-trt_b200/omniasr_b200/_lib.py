@@ -52,6 +52,8 @@ SIGNATURES = {
                              _i, _p, _p]),
     "omniasr_beam_select": (_i, [_p, _i64, _i, _p, _p, _p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _i, _i,
                                  _i, _i64, _i64, _i64, _p, _p]),
+    "omniasr_decode_gemm_rope": (_i, [_p, _i64, _i, _p, _i64, _i, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                                      _i64, _i64, _i, _i, _p, _sz, _p, _p]),
     "omniasr_accept": (_i, [_p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i, _i, _i64, _i64, _p, _p]),
     "omniasr_decode_gemm_workspace": (_sz, [_i, _i, _i, _i]),
     "omniasr_decode_gemm": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _i, _p, _i64, _p, _i64, _p, _sz, _p, _p]),

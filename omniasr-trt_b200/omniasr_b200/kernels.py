@@ -433,6 +433,37 @@ def decode_gemm(x: torch.Tensor, w: torch.Tensor, mode: str = "store", residual:
     return out
 
 
+def decode_gemm_rope(x: torch.Tensor, w: torch.Tensor, cs: torch.Tensor, pos: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor, heads: int, slots: torch.Tensor | None = None,
+                     cache_pos: torch.Tensor | None = None) -> torch.Tensor:
+    """``rope_kv(x @ w.t(), cs, pos, k_cache, v_cache, heads, slots, cache_pos)`` in one kernel (bf16, at most 64
+    token rows, head_dim a multiple of 128): the QKV product's epilogue rotates q and k and appends k and v to the
+    caches; returns q [N, heads, D]. The product is rounded to bf16 before the rotation, as the GEMM's output is."""
+    rows, k = x.shape
+    n = w.size(0)
+    dim = n // (3 * heads)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.size(1) != k or n != 3 * heads * dim:
+        raise ValueError("decode_gemm_rope: bf16 x [rows, k], w [3 * heads * D, k]")
+    if x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("decode_gemm_rope: unit inner strides")
+    q = torch.empty(rows, heads, dim, dtype=x.dtype, device=x.device)
+    if rows == 0:
+        return q
+    if k_cache.dtype != x.dtype:
+        raise ValueError("decode_gemm_rope: cache dtype differs from x")
+    cs = cs if cs.dtype == torch.float32 and cs.is_contiguous() else cs.float().contiguous()
+    crows, length, s_row, s_head, s_pos = _cache(k_cache, v_cache, "decode_gemm_rope")
+    pos = _index(pos)
+    slots = None if slots is None else _index(slots)
+    cache_pos = None if cache_pos is None else _index(cache_pos)
+    lib = _lib.load()
+    ws = _gemm_workspace(lib.omniasr_decode_gemm_workspace(rows, n, k, GEMM_MODES["store"]), x.device)
+    _lib.call("omniasr_decode_gemm_rope", _ptr(x), x.stride(0), rows, _ptr(w), w.stride(0), k, _ptr(cs), cs.size(0),
+              _ptr(pos), _ptr(slots), _ptr(cache_pos), _ptr(q), _ptr(k_cache), _ptr(v_cache), crows, length, s_row,
+              s_head, s_pos, heads, dim, _ptr(ws), ws.numel(), _ptr(status_word(x.device)), _stream(x.device))
+    return q
+
+
 def reorder_gather(src: torch.Tensor, parent: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``out[r] = src[parent[r]]`` along dim 0, byte-exact (``torch.index_select(src, 0, parent)``); each row of
     ``src`` / ``out`` must be contiguous. ``out`` (optional) must not overlap ``src``."""
