@@ -58,7 +58,14 @@ struct Smem {
 // Warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads, 7 write-out; with head_dim 512 also warp 8, which
 // zeroes the V rows past a unit's keys in its last tile (the key tile's four 128-dim chunks stream through the ring,
 // so the softmax warps, which did this for head_dim 128, cannot wait for all of them).
-constexpr int threads_for(int dim) { return dim == 128 ? 256 : 288; }
+// With split issue (head_dim 512; head_dim 128 with OMNI_TC_SPLIT_128) the O^T MMAs have their own issuing thread
+// (the last warp), so that the S^T MMAs of later tiles never wait behind the V chunks of an earlier one.
+#ifndef OMNI_TC_SPLIT_128
+#define OMNI_TC_SPLIT_128 0
+#endif
+constexpr bool split_issue(int dim) { return dim == 512 || OMNI_TC_SPLIT_128; }
+constexpr int pv_warp(int dim) { return dim == 128 ? 8 : 9; }
+constexpr int threads_for(int dim) { return 32 * (split_issue(dim) ? pv_warp(dim) + 1 : (dim == 128 ? 8 : 9)); }
 // TMEM: S^T x2 (cols 0-31), then O^T x2 per 128-dim chunk of the head (16 columns each).
 constexpr uint32_t tmem_cols(int dim) { return dim == 128 ? 64u : 256u; }
 OMNI_DEV uint32_t ocol(int buf, int chunk, int dc) { return 2 * NQP + (buf * dc + chunk) * NQP; }
@@ -502,7 +509,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
       mbar_init(&q_fill[s], 1);
       mbar_init(&q_done[s], 1);
     }
-    mbar_init(&drain, 1);
+    mbar_init(&drain, split_issue(DIM) ? 2 : 1);
     mbar_init(&seg_ready, 128);
     mbar_init(&seg_free, 1);
     for (int c = 0; c < DC; ++c) {
@@ -662,9 +669,44 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 5 || (split_issue(DIM) && warp == pv_warp(DIM))) {
+    // ------------------------------------------------------------------ MMA issuer(s)
+    if (lane == 0 && warp == pv_warp(DIM)) {
+      // ---------------------------------------------------------------- O^T issuer (split issue)
+      TileIter ti = first_tile;
+      int unit = -1;
+      (void)unit;
+      // O^T(t) = V(t)^T P^T(t), one accumulator per 128-dim chunk. tail: the index of this tile among the CTA's last
+      // tiles of units (head_dim 512: its V chunks wait until warp 8 has zeroed their stale rows), or -1.
+      auto values = [&](int t, int tail) -> bool {
+        const int b = t & 1, u = t >> 1;
+        if (u >= 1 && !mbar_wait(&o_free[b], (u - 1) & 1)) return false;
+        if (!mbar_wait(&p_full[b], u & 1)) return false;
+#pragma unroll 1
+        for (int c = 0; c < DC; ++c) {
+          const int ci = t * DC + c;
+          const int slot = HALF + ci % HALF;
+          if (DC > 1 && tail >= 0) {
+            if (!mbar_wait(&vfix[c], tail & 1)) return false;
+          } else if (!mbar_wait(&full[slot], (ci / HALF) & 1)) {
+            return false;
+          }
+          tc_fence_after();
+          if (c == 0) OMNI_TRACE_AT(t * 8 + 3);
+          issue_values(tbase, ocol(b, c, DC), smem + slot * SLOT_BYTES, smem + L::P_OFF + b * (NQP * BN * 2));
+          if (c == DC - 1) tc_commit(&o_full[b]);
+          tc_commit(&empty[slot]);
+        }
+        return true;
+      };
+      bool ok = true;
+      int tails = 0;
+      for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
+        const int tail = DC > 1 && (int64_t)ti.t * BN + BN > ti.need ? tails++ : -1;
+        ok = values(it, tail);
+      }
+      if (!ok) abort_flag = 1;
+    } else if (lane == 0) {
       TileIter ti = first_tile;
       int unit = -1;
       auto scores = [&](int t) -> bool {  // S^T(t) = K(t) Q^T, accumulated over the head's 128-dim chunks
@@ -706,24 +748,36 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
         }
         return true;
       };
-      // Tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1) runs -- also
-      // across a unit boundary, where the softmax finishes the old unit one tile late.
       bool ok = true;
-      int pend = -1;       // tile whose O^T is still to issue
-      int pend_tail = -1;  // its index among the last tiles of units (head_dim 512), or -1
-      int tails = 0;
-      for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
-        if (ti.t == 0 || it == 0) {
-          ++unit;
-          if (!mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
+      if constexpr (split_issue(DIM)) {
+        // S^T only: the O^T issuer (warp pv_warp) walks the same tiles on its own.
+        for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
+          if (ti.t == 0 || it == 0) {
+            ++unit;
+            if (!mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
+          }
+          if (ok) ok = scores(it);
+          if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
         }
-        if (ok) ok = scores(it);
-        if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
-        if (ok && pend >= 0) ok = values(pend, pend_tail);
-        pend = it;
-        pend_tail = DC > 1 && (int64_t)ti.t * BN + BN > ti.need ? tails++ : -1;
+      } else {
+        // Tile t's S^T goes out before tile t-1's O^T, so the softmax of t can start while O^T(t-1) runs -- also
+        // across a unit boundary, where the softmax finishes the old unit one tile late.
+        int pend = -1;       // tile whose O^T is still to issue
+        int pend_tail = -1;  // its index among the last tiles of units (head_dim 512), or -1
+        int tails = 0;
+        for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
+          if (ti.t == 0 || it == 0) {
+            ++unit;
+            if (!mbar_wait(&q_fill[unit & 1], (unit >> 1) & 1)) ok = false;
+          }
+          if (ok) ok = scores(it);
+          if (ok && ti.last_here()) tc_commit(&q_done[unit & 1]);  // the unit's last S^T in this CTA
+          if (ok && pend >= 0) ok = values(pend, pend_tail);
+          pend = it;
+          pend_tail = DC > 1 && (int64_t)ti.t * BN + BN > ti.need ? tails++ : -1;
+        }
+        if (ok && pend >= 0 && !abort_flag) ok = values(pend, pend_tail);
       }
-      if (ok && pend >= 0 && !abort_flag) ok = values(pend, pend_tail);
       if (!ok) abort_flag = 1;
     }
     __syncwarp();
@@ -1096,8 +1150,8 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
   if (tid == 0) OMNI_TRACE_AT(4020);
   if (abort_flag) {
     if (tid == 0) raise_status(p.status, kStatusTimeout);
-    if (tid == 5 * 32) {
-      tc_commit(&drain);  // every MMA the issuer thread issued has completed once this arrives
+    if (tid == 5 * 32 || (split_issue(DIM) && tid == pv_warp(DIM) * 32)) {
+      tc_commit(&drain);  // every MMA the issuer thread(s) issued has completed once these arrive
       mbar_wait(&drain, 0);
     }
     if (tid == 4 * 32) {
