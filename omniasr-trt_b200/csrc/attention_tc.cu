@@ -58,14 +58,18 @@ struct Smem {
 // Warps 0-3 softmax, 4 K + query loads, 5 MMA issuer, 6 V loads, 7 write-out; with head_dim 512 also warp 8, which
 // zeroes the V rows past a unit's keys in its last tile (the key tile's four 128-dim chunks stream through the ring,
 // so the softmax warps, which did this for head_dim 128, cannot wait for all of them).
-// With split issue (head_dim 512; head_dim 128 with OMNI_TC_SPLIT_128) the O^T MMAs have their own issuing thread
-// (the last warp), so that the S^T MMAs of later tiles never wait behind the V chunks of an earlier one.
-#ifndef OMNI_TC_SPLIT_128
-#define OMNI_TC_SPLIT_128 0
+// With split issue the O^T MMAs have their own issuing thread (the last warp), so that the S^T MMAs of later tiles
+// never wait behind the V chunks of an earlier one: head_dim 512, and head_dim 128 up to OMNI_TC_SPLIT_NQ queries per
+// unit (measured at head_dim 128, three runs each on one box: decode 4804 -> 4869 GB/s with one query; verify, 8
+// query columns, 4232 -> 3968).
+#ifndef OMNI_TC_SPLIT_NQ
+#define OMNI_TC_SPLIT_NQ 2
 #endif
-constexpr bool split_issue(int dim) { return dim == 512 || OMNI_TC_SPLIT_128; }
+constexpr bool split_issue(int dim, int nqt) { return dim == 512 || nqt <= OMNI_TC_SPLIT_NQ; }
 constexpr int pv_warp(int dim) { return dim == 128 ? 8 : 9; }
-constexpr int threads_for(int dim) { return 32 * (split_issue(dim) ? pv_warp(dim) + 1 : (dim == 128 ? 8 : 9)); }
+constexpr int threads_for(int dim, int nqt) {
+  return 32 * (split_issue(dim, nqt) ? pv_warp(dim) + 1 : (dim == 128 ? 8 : 9));
+}
 // TMEM: S^T x2 (cols 0-31), then O^T x2 per 128-dim chunk of the head (16 columns each).
 constexpr uint32_t tmem_cols(int dim) { return dim == 128 ? 64u : 256u; }
 OMNI_DEV uint32_t ocol(int buf, int chunk, int dc) { return 2 * NQP + (buf * dc + chunk) * NQP; }
@@ -467,13 +471,13 @@ OMNI_DEV void issue_values(uint32_t tbase, uint32_t dcol, const unsigned char* v
 // over the K chunks, O^T has one accumulator per V chunk. With more than one chunk, warp 8 zeroes the V rows past a
 // unit's keys in each chunk of its last tile (vfix[c] <- zeroed) before the MMA reads them.
 template <int NQT, int SLOTS, int DIM>
-__global__ void __launch_bounds__(threads_for(DIM), 1)
+__global__ void __launch_bounds__(threads_for(DIM, NQT), 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap_half,
                    const __grid_constant__ CUtensorMap vmap_half, const Params pin) {
   using L = Smem<SLOTS, DIM>;
   constexpr int DC = DIM / D;  // 128-dim chunks per head
-  constexpr int THREADS = threads_for(DIM);
+  constexpr int THREADS = threads_for(DIM, NQT);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -509,7 +513,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
       mbar_init(&q_fill[s], 1);
       mbar_init(&q_done[s], 1);
     }
-    mbar_init(&drain, split_issue(DIM) ? 2 : 1);
+    mbar_init(&drain, split_issue(DIM, NQT) ? 2 : 1);
     mbar_init(&seg_ready, 128);
     mbar_init(&seg_free, 1);
     for (int c = 0; c < DC; ++c) {
@@ -669,7 +673,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5 || (split_issue(DIM) && warp == pv_warp(DIM))) {
+  } else if (warp == 5 || (split_issue(DIM, NQT) && warp == pv_warp(DIM))) {
     // ------------------------------------------------------------------ MMA issuer(s)
     if (lane == 0 && warp == pv_warp(DIM)) {
       // ---------------------------------------------------------------- O^T issuer (split issue)
@@ -749,7 +753,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
         return true;
       };
       bool ok = true;
-      if constexpr (split_issue(DIM)) {
+      if constexpr (split_issue(DIM, NQT)) {
         // S^T only: the O^T issuer (warp pv_warp) walks the same tiles on its own.
         for (int it = 0; !ti.done && ok && !abort_flag; ++it, ti.advance()) {
           if (ti.t == 0 || it == 0) {
@@ -1150,7 +1154,7 @@ __global__ void __launch_bounds__(threads_for(DIM), 1)
   if (tid == 0) OMNI_TRACE_AT(4020);
   if (abort_flag) {
     if (tid == 0) raise_status(p.status, kStatusTimeout);
-    if (tid == 5 * 32 || (split_issue(DIM) && tid == pv_warp(DIM) * 32)) {
+    if (tid == 5 * 32 || (split_issue(DIM, NQT) && tid == pv_warp(DIM) * 32)) {
       tc_commit(&drain);  // every MMA the issuer thread(s) issued has completed once these arrive
       mbar_wait(&drain, 0);
     }
@@ -1393,6 +1397,9 @@ int tc_segments(int64_t keys) { return (int)((keys + tcattn::BN - 1) / tcattn::B
 
 int tc_grid() { return device_sm_count(); }
 
+// The pass instance's query columns for nq queries per unit (1, 2, 4, 8 or 16).
+int tc_nqt(int nq) { return nq <= 1 ? 1 : nq <= 2 ? 2 : nq <= 4 ? 4 : nq <= 8 ? 8 : 16; }
+
 // Tiles the producers prefetch into L2 ahead of their loads (OMNIASR_TC_PREFETCH overrides the default).
 int tc_prefetch() {
   static const int n = [] {
@@ -1492,7 +1499,7 @@ cudaError_t launch_tc_pass(const void* k, const void* v, int64_t cache_rows, int
   // Programmatic dependent launch: the set-up above griddepcontrol.wait overlaps the previous kernel.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
-  cfg.blockDim = dim3(threads_for(p.dim));
+  cfg.blockDim = dim3(threads_for(p.dim, tc_nqt(p.nq)));
   cfg.dynamicSmemBytes = (size_t)bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
