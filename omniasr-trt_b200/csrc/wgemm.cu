@@ -8,11 +8,15 @@
 //
 // Schedule: persistent stream-K. The (weight tile, 64-wide K chunk) units, tile-major, are cut into one contiguous
 // range per CTA (one CTA per SM), so every SM streams the same number of weight bytes whatever n. A tile whose
-// chunks one CTA covers completely is finished by that CTA's epilogue; a tile cut between CTAs leaves an fp32
-// partial per CTA (slot 0: the CTA's first tile, slot 1: its last), and the last of those CTAs to finish (a per-tile
-// arrival counter in the workspace) sums them and runs the same epilogue, then sets the counter back to zero -- so
-// the counters are zero before and after every call, and no second kernel is needed. Roles (192 threads): warp 0 TMA (weight box + token box per stage, 8-stage ring), warp 1 MMA
-// issuer, warps 2-5 epilogue (thread = weight row = TMEM lane).
+// chunks one CTA covers completely is finished by that CTA's epilogue. A tile cut between CTAs leaves an fp32 partial
+// per contributor (slot 0: the CTA's first tile, slot 1: its last), summed in one fixed order whoever finishes the
+// tile. A CTA's last range usually begins a tile whose other contributors worked on it first (at the start of their
+// ranges): such a CTA watches the tile's arrival counter while its last MMAs run, sums the others' partials as soon
+// as they are all in, and finishes the tile with its own accumulator as the last term -- so the end of a call
+// carries no chain of global round trips. Otherwise the last contributor to arrive sums the slots. The finishing CTA
+// sets the counter back to zero, so the counters are zero before and after every call and no second kernel is
+// needed. Roles (192 threads): warp 0 TMA (weight boxes + token boxes per stage), warp 1 MMA issuer, warps 2-5
+// epilogue (thread = weight row = TMEM lane).
 //
 // SwiGLU: the gate and inner rows of the same 64 outputs are two 64-row boxes of one 128-row tile (no weight copy),
 // so the epilogue forms inner * silu(gate) within the tile.
@@ -23,6 +27,15 @@
 #include "common.cuh"
 #include "tc.cuh"
 #include "wgemm.cuh"
+
+// Pipeline events of every CTA (entry, after the dependency wait, first load issued, first stage landed, last MMA
+// issued, last accumulator handed over, epilogue done, exit), for a tracing harness that defines this hook before it
+// includes this file; product builds compile it to nothing.
+#ifndef OMNI_WG_EVENT
+#define OMNI_WG_EVENT(args, ev) \
+  do {                          \
+  } while (0)
+#endif
 
 namespace omni {
 
@@ -37,6 +50,12 @@ constexpr int KB = OMNI_WGEMM_KB;  // boxes per stage along K: each weight row g
 constexpr int BKU = BK * KB;       // K per unit (chunk)
 constexpr int W_BOX = BM * BK * 2;
 constexpr int W_BYTES = KB * W_BOX;
+#ifndef OMNI_WGEMM_PREFETCH
+#define OMNI_WGEMM_PREFETCH 0
+#endif
+#ifndef OMNI_WGEMM_EARLY_TRIGGER
+#define OMNI_WGEMM_EARLY_TRIGGER 0
+#endif
 #ifndef OMNI_WGEMM_STAGES
 #define OMNI_WGEMM_STAGES (8 / OMNI_WGEMM_KB)
 #endif
@@ -48,12 +67,18 @@ struct Layout {
   static constexpr int X_BOX = NT * BK * 2;
   static constexpr int X_BYTES = KB * X_BOX;
   static constexpr int STAGE = W_BYTES + X_BYTES;  // a multiple of 1024 for NT in {16, 32, 48, 64}
-  static constexpr int XCH_OFF = STAGES * STAGE;   // SwiGLU exchange [64][NT] fp32
-  static constexpr int BYTES = XCH_OFF + 64 * NT * 4 + 1024;
+  static constexpr int XCH_OFF = STAGES * STAGE;   // epilogue staging [NT][128] fp32
+  static constexpr int BYTES = XCH_OFF + NT * BM * 4 + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * NT <= 32 ? 32 : (2 * NT <= 64 ? 64 : 128);
 };
 
 OMNI_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+OMNI_DEV int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // kGemmRope: a token's place, staged in shared memory once per CTA by the epilogue threads (thread m = token m):
 // the offset of its cos/sin row (-1: position outside the table) and of its cache slot (-1: outside the cache).
@@ -80,29 +105,6 @@ OMNI_DEV void stage_tokens(const GemmArgs& a, int m, TokenPlace* place) {
 // of the 128 participating threads, which all call this together (named barrier `bar`).
 template <int NT, int MODE>
 OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&acc)[NT], float* xch, int bar) {
-  if (MODE == kGemmSwiglu) {
-    if (row >= 64) {
-#pragma unroll
-      for (int m = 0; m < NT; ++m) xch[(row - 64) * NT + m] = acc[m];
-    }
-    named_sync(bar, 128);
-    if (row < 64) {
-      const int f = tile * 64 + row;
-      if (f < a.n) {
-#pragma unroll
-        for (int m = 0; m < NT; ++m) {
-          if (m < a.rows) {
-            const float g = bf16r(acc[m]);
-            const float u = bf16r(xch[row * NT + m]);
-            const float s = bf16r(g / (1.f + __expf(-g)));
-            a.y[(int64_t)m * a.ld_y + f] = __float2bfloat16_rn(u * s);
-          }
-        }
-      }
-    }
-    named_sync(bar, 128);  // xch free again
-    return;
-  }
   if (MODE == kGemmRope) {
     // Feature f = tile * 128 + row is head dim d of head h of section q / k / v (128 divides the head_dim, so a
     // rotation pair (2j, 2j + 1) never straddles two tiles: its partner is the neighbouring lane). Each product is
@@ -155,23 +157,80 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
     }
     return;
   }
-  const int n = tile * BM + row;
-  if (n >= a.n) return;
-  float v[NT];
+  // Store / residual / SwiGLU: the tile goes through shared memory (`xch`, [NT][128] fp32, thread `row` writes
+  // column `row`), then each thread writes 16-byte runs of 8 outputs of one token row -- one vector store (and one
+  // vector residual load, all of a thread's loads issued before its first store, since y may be the residual) per 8
+  // outputs instead of one 2-byte store per output. SwiGLU: columns 0..63 are the gate and 64..127 the inner
+  // products of outputs tile * 64 + c, each rounded to bf16 before inner * silu(gate).
 #pragma unroll
-  for (int m = 0; m < NT; ++m) v[m] = acc[m];
+  for (int m = 0; m < NT; ++m) xch[m * BM + row] = acc[m];
+  named_sync(bar, 128);
+  constexpr int WIDTH = MODE == kGemmSwiglu ? 64 : BM;  // outputs of one tile
+  constexpr int RUNS = WIDTH / 8;                       // 16-byte runs per token row
+  constexpr int MAXK = (NT * RUNS + 127) / 128;         // runs per thread
+  const int64_t col0 = (int64_t)tile * WIDTH;
+  const int cols = (int)min((int64_t)WIDTH, (int64_t)a.n - col0);
+  const bool vec_y = (a.ld_y & 7) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  const bool vec_r = MODE != kGemmResidual || ((a.ld_res & 7) == 0 && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0);
+  const int runs = a.rows * RUNS;
+  uint4 res[MAXK];
   if (MODE == kGemmResidual) {
-    // Every residual load before the first store: y may be the residual itself (in place), so a store could
-    // not be moved past a later load, and interleaving them would serialise the loads' latencies.
-    __nv_bfloat16 r[NT];
 #pragma unroll
-    for (int m = 0; m < NT; ++m) r[m] = m < a.rows ? a.residual[(int64_t)m * a.ld_res + n] : __float2bfloat16_rn(0.f);
+    for (int k = 0; k < MAXK; ++k) {
+      const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
+      res[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (c < runs) {
+        const __nv_bfloat16* src = a.residual + (int64_t)m * a.ld_res + col0 + j0;
+        if (vec_r && j0 + 8 <= cols) {
+          res[k] = *reinterpret_cast<const uint4*>(src);
+        } else {
+          __nv_bfloat16* r8 = reinterpret_cast<__nv_bfloat16*>(&res[k]);
 #pragma unroll
-    for (int m = 0; m < NT; ++m) v[m] += __bfloat162float(r[m]);
+          for (int q = 0; q < 8; ++q)
+            if (j0 + q < cols) r8[q] = src[q];
+        }
+      }
+    }
   }
 #pragma unroll
-  for (int m = 0; m < NT; ++m)
-    if (m < a.rows) a.y[(int64_t)m * a.ld_y + n] = __float2bfloat16_rn(v[m]);
+  for (int k = 0; k < MAXK; ++k) {
+    const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
+    if (c >= runs) break;
+    const float4* src = reinterpret_cast<const float4*>(xch + m * BM + j0);
+    float v[8];
+    if (MODE == kGemmSwiglu) {
+      const float4 g0 = src[0], g1 = src[1], u0 = src[16], u1 = src[17];  // inner products: 64 columns on
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float gq = bf16r(g[q]);
+        const float sq = bf16r(gq / (1.f + __expf(-gq)));
+        v[q] = bf16r(u[q]) * sq;
+      }
+    } else {
+      const float4 v0 = src[0], v1 = src[1];
+      v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w, v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
+      if (MODE == kGemmResidual) {
+        const __nv_bfloat16* r8 = reinterpret_cast<const __nv_bfloat16*>(&res[k]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] += __bfloat162float(r8[q]);
+      }
+    }
+    uint4 out;
+    __nv_bfloat16* o8 = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o8[q] = __float2bfloat16_rn(v[q]);
+    __nv_bfloat16* dst = a.y + (int64_t)m * a.ld_y + col0 + j0;
+    if (vec_y && j0 + 8 <= cols) {
+      *reinterpret_cast<uint4*>(dst) = out;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (j0 + q < cols) dst[q] = o8[q];
+    }
+  }
+  named_sync(bar, 128);  // xch free again
 }
 
 template <int NT, int MODE>
@@ -189,6 +248,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   int* last_flag = &last_flag_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) OMNI_WG_EVENT(a, 0);
   const int64_t total = (int64_t)a.tiles * a.chunks;
   const int64_t u0 = (int64_t)blockIdx.x * a.per;
   const int64_t u1 = min(total, u0 + a.per);
@@ -216,37 +276,63 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+
+  // The weight boxes of stage i (unit u) and its token boxes; stage i's `full` barrier expects both.
+  auto load_w = [&](int i, int64_t u) {
+    const int t = (int)(u / a.chunks), c = (int)(u % a.chunks);
+    unsigned char* st = smem + (i % STAGES) * L::STAGE;
+    uint64_t* bar = &full[i % STAGES];
+    mbar_arrive_expect_tx(bar, L::STAGE);
+#pragma unroll
+    for (int j = 0; j < KB; ++j) {  // the weight boxes back to back: each row's KB * 128 bytes together
+      const int kx = c * BKU + j * BK;
+      if (MODE == kGemmSwiglu) {
+        tma_load_2d(st + j * W_BOX, &wmap, kx, t * 64, bar);                   // gate rows
+        tma_load_2d(st + j * W_BOX + W_BOX / 2, &wmap, kx, a.n + t * 64, bar);  // inner rows
+      } else {
+        tma_load_2d(st + j * W_BOX, &wmap, kx, t * BM, bar);
+      }
+    }
+  };
+  auto load_x = [&](int i, int64_t u) {
+    const int c = (int)(u % a.chunks);
+    unsigned char* st = smem + (i % STAGES) * L::STAGE;
+#pragma unroll
+    for (int j = 0; j < KB; ++j) tma_load_2d(st + W_BYTES + j * L::X_BOX, &xmap, c * BKU + j * BK, 0, &full[i % STAGES]);
+  };
+  // The weights do not depend on the kernel before: the first stages' weight boxes are requested before the
+  // dependency wait, so their latency overlaps that kernel's tail.
+  int pre = 0;
+#if OMNI_WGEMM_PREFETCH
+  if (warp == 0 && lane == 0) {
+    for (; pre < STAGES && u0 + pre < u1; ++pre) load_w(pre, u0 + pre);
+    OMNI_WG_EVENT(a, 2);
+  }
+#endif
   grid_dependency_wait();  // the tokens come from the kernel before (launched as a programmatic dependent)
+  if (tid == 0) OMNI_WG_EVENT(a, 1);
   const uint32_t tbase = tmem_base;
-  const int first_tile = (int)(u0 / a.chunks);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int i = 0;
-      for (int64_t u = u0; u < u1 && !abort_flag; ++u, ++i) {
-        const int t = (int)(u / a.chunks), c = (int)(u % a.chunks);
+      for (; i < pre; ++i) load_x(i, u0 + i);  // the token boxes of the prefetched stages, whatever happens next
+      issued = pre;
+      for (int64_t u = u0 + pre; u < u1 && !abort_flag; ++u, ++i) {
         const int s = i % STAGES, use = i / STAGES;
         if (use >= 1 && !mbar_wait(&empty[s], (use - 1) & 1)) {
           abort_flag = 1;
           break;
         }
-        unsigned char* st = smem + s * L::STAGE;
-        mbar_arrive_expect_tx(&full[s], L::STAGE);
-#pragma unroll
-        for (int j = 0; j < KB; ++j) {  // the weight boxes back to back: each row's KB * 128 bytes together
-          const int kx = c * BKU + j * BK;
-          if (MODE == kGemmSwiglu) {
-            tma_load_2d(st + j * W_BOX, &wmap, kx, t * 64, &full[s]);                   // gate rows
-            tma_load_2d(st + j * W_BOX + W_BOX / 2, &wmap, kx, a.n + t * 64, &full[s]);  // inner rows
-          } else {
-            tma_load_2d(st + j * W_BOX, &wmap, kx, t * BM, &full[s]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < KB; ++j) tma_load_2d(st + W_BYTES + j * L::X_BOX, &xmap, c * BKU + j * BK, 0, &full[s]);
+        load_w(i, u);
+        load_x(i, u);
+        if (i == 0) OMNI_WG_EVENT(a, 2);
         issued = i + 1;
       }
+#if OMNI_WGEMM_EARLY_TRIGGER
+      grid_launch_dependents();  // every load issued: the next kernel's blocks may take free SMs and prefetch
+#endif
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -270,6 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
+        if (i == 0) OMNI_WG_EVENT(a, 3);
         const uint32_t wa = smem_addr(smem + s * L::STAGE), xa = wa + W_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BKU / 16; ++kk) {
@@ -284,6 +371,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) abort_flag = 1;
+      OMNI_WG_EVENT(a, 4);
     }
     __syncwarp();
   } else {
@@ -301,7 +389,59 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t seg_end = min(u1, (int64_t)(t + 1) * a.chunks);  // exclusive
       const bool whole = c0 == 0 && seg_end == (int64_t)(t + 1) * a.chunks;
       const int buf = seg & 1;
+      // A split tile's contributors are CTAs b0..b1; each leaves its fp32 partial in its own slot and the tile is
+      // summed in one fixed order, p[b1] + p[b1 - 1] + ... + p[b0], whoever finishes it, so results do not depend
+      // on timing. The contributor that begins the tile (b0: the last range of its CTA, while the others met the
+      // tile at the start of theirs) watches the tile's counter while its accumulator is still being computed; once
+      // every other contributor has arrived it sums their partials ahead of its own and finishes the tile with its
+      // accumulator as the last term, without publishing it -- so the end of a call carries no chain of global
+      // round trips. Otherwise the last contributor to arrive sums the slots.
+      const int64_t tc0 = (int64_t)t * a.chunks;
+      const int me = blockIdx.x;
+      const int b0 = (int)(tc0 / a.per), b1 = (int)((tc0 + a.chunks - 1) / a.per);
+      auto slot_of = [&](int b) -> const float4* {
+        const int sl = t == (int)(((int64_t)b * a.per) / a.chunks) ? 0 : 1;
+        return reinterpret_cast<const float4*>(a.part) + ((int64_t)(b * 2 + sl) * (NT / 4)) * BM + row;
+      };
+      float others[NT];
+      bool early = false;
+      if (!whole && me == b0) {
+        const uint64_t t0 = global_ns();
+        int f = 0;
+        do {
+          if (row == 0) {
+            // a relaxed poll; the fence below orders the partial loads after the arrivals it saw
+            int v = ld_relaxed_gpu(&a.counters[t]) == b1 - b0 ? 1 : 0;
+            if (!v && mbar_test_wait(&acc_full[buf], (seg >> 1) & 1)) v = 2;
+            if (!v && global_ns() - t0 > kWaitLimitNs) v = 3;
+            *last_flag = v;
+          }
+          named_sync(2, 128);
+          f = *last_flag;
+          named_sync(2, 128);
+          if (f == 0 && row == 0) __nanosleep(200);
+        } while (f == 0);
+        OMNI_WG_EVENT(a, 8 + f);
+        if (f == 3) abort_flag = 1;
+        early = f == 1;
+        if (early) {
+          __threadfence();
+          for (int b = b1; b > b0; --b) {
+            const float4* src = slot_of(b);
+#pragma unroll
+            for (int m = 0; m < NT; m += 4) {
+              const float4 v = __ldcg(src + (m / 4) * BM);  // other CTAs' stores: from L2
+              if (b == b1) {
+                others[m] = v.x, others[m + 1] = v.y, others[m + 2] = v.z, others[m + 3] = v.w;
+              } else {
+                others[m] += v.x, others[m + 1] += v.y, others[m + 2] += v.z, others[m + 3] += v.w;
+              }
+            }
+          }
+        }
+      }
       if (!mbar_wait(&acc_full[buf], (seg >> 1) & 1)) abort_flag = 1;
+      if (tid == 64 && seg_end == u1) OMNI_WG_EVENT(a, 5);
       tc_fence_after();
       __syncwarp();
       float acc[NT];
@@ -311,42 +451,55 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&acc_free[buf]);
       if (whole) {
         finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
-      } else {
-        const int slot = t == first_tile ? 0 : 1;
-        float* dst = a.part + (((int64_t)blockIdx.x * 2 + slot) * BM + row) * NT;
+      } else if (early) {
 #pragma unroll
-        for (int m = 0; m < NT; m += 4) *reinterpret_cast<float4*>(dst + m) = make_float4(acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
-        // Arrive on the tile's counter; the last CTA to arrive sums every covering CTA's partial and finishes it.
+        for (int m = 0; m < NT; ++m) acc[m] = others[m] + acc[m];
+        if (tid == 64) OMNI_WG_EVENT(a, 12);
+        finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
+        if (tid == 64) OMNI_WG_EVENT(a, 13);
+        if (row == 0) a.counters[t] = 0;  // zero again for the next call
+      } else {
+        float4* dst = const_cast<float4*>(slot_of(me));
+#pragma unroll
+        for (int m = 0; m < NT; m += 4) dst[(m / 4) * BM] = make_float4(acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
         __threadfence();
         named_sync(2, 128);
-        const int64_t c0 = (int64_t)t * a.chunks;
-        const int b0 = (int)(c0 / a.per), b1 = (int)((c0 + a.chunks - 1) / a.per);
         if (row == 0) *last_flag = atomicAdd(&a.counters[t], 1) == b1 - b0;
         named_sync(2, 128);
+        if (tid == 64) OMNI_WG_EVENT(a, 14);
         if (*last_flag) {
           __threadfence();
-          float sum[NT];
+          // Two slots per round trip, summed in the fixed order.
+          for (int b = b1; b >= b0; b -= 2) {
+            const float4* s0 = slot_of(b);
+            const float4* s1 = slot_of(b > b0 ? b - 1 : b);
+            float4 v0[NT / 4], v1[NT / 4];
 #pragma unroll
-          for (int m = 0; m < NT; ++m) sum[m] = 0.f;
-          for (int b = b0; b <= b1; ++b) {
-            const int sl = t == (int)(((int64_t)b * a.per) / a.chunks) ? 0 : 1;
-            const float4* src = reinterpret_cast<const float4*>(a.part + (((int64_t)b * 2 + sl) * BM + row) * NT);
+            for (int m = 0; m < NT / 4; ++m) {
+              v0[m] = __ldcg(s0 + m * BM);
+              v1[m] = __ldcg(s1 + m * BM);
+            }
 #pragma unroll
-            for (int m = 0; m < NT; m += 4) {
-              const float4 v = __ldcg(src + m / 4);  // other CTAs' stores: from L2, not a stale L1 line
-              sum[m] += v.x;
-              sum[m + 1] += v.y;
-              sum[m + 2] += v.z;
-              sum[m + 3] += v.w;
+            for (int m = 0; m < NT / 4; ++m) {
+              if (b == b1) {
+                acc[4 * m] = v0[m].x, acc[4 * m + 1] = v0[m].y, acc[4 * m + 2] = v0[m].z, acc[4 * m + 3] = v0[m].w;
+              } else {
+                acc[4 * m] += v0[m].x, acc[4 * m + 1] += v0[m].y, acc[4 * m + 2] += v0[m].z, acc[4 * m + 3] += v0[m].w;
+              }
+              if (b > b0) {
+                acc[4 * m] += v1[m].x, acc[4 * m + 1] += v1[m].y, acc[4 * m + 2] += v1[m].z, acc[4 * m + 3] += v1[m].w;
+              }
             }
           }
-          finish_tile<NT, MODE>(a, t, row, sum, xch, 1);
+          if (tid == 64) OMNI_WG_EVENT(a, 15);
+          finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
           if (row == 0) a.counters[t] = 0;  // zero again for the next call
         }
       }
       u = seg_end;
       if (abort_flag) break;
     }
+    if (tid == 64) OMNI_WG_EVENT(a, 6);
   }
   __syncthreads();
   if (abort_flag) {
@@ -367,6 +520,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tbase, L::TMEM_COLS);
   }
+  if (tid == 0) OMNI_WG_EVENT(a, 7);
   grid_launch_dependents();
 }
 

@@ -24,7 +24,7 @@ struct GemmArgs {
   int64_t ld_res;
   __nv_bfloat16* y;
   int64_t ld_y;
-  float* part;    // [grid, 2, 128, NT] fp32 partial tiles of weight tiles split between CTAs
+  float* part;    // [grid, 2, NT / 4, 128, 4] fp32 partials of weight tiles split between CTAs
   int* counters;  // [tiles] arrivals on split tiles: zero before and after a call
   int tiles, chunks, grid;
   int64_t per;  // (tile, chunk) units per CTA

@@ -64,8 +64,8 @@ def status_word(device: torch.device | int | None = None) -> torch.Tensor:
 
 def read_status(device=None, clear: bool = True) -> int:
     """Synchronises, returns the status word and clears it. After a wait that gave up (bit 2) the unit counters of
-    the decode / draft workspaces may be left non-zero, so those workspaces are dropped (the next call zeroes a
-    new one)."""
+    the decode / draft workspaces and the split-tile counters and sums of the GEMM workspaces may be left non-zero,
+    so those workspaces are dropped (the next call zeroes a new one)."""
     word = status_word(device)
     value = int(word.item())
     if clear:
@@ -74,6 +74,8 @@ def read_status(device=None, clear: bool = True) -> int:
         index = word.device.index
         for key in [k for k in _ATTN_WS if k[0] == index]:
             _ATTN_WS_RETIRED.append(_ATTN_WS.pop(key))
+        for key in [k for k in _GEMM_WS if k[0] == index]:
+            _GEMM_WS_RETIRED.append(_GEMM_WS.pop(key))
     return value
 
 
@@ -389,7 +391,7 @@ def beam_select(logp: torch.Tensor, score: torch.Tensor, ended: torch.Tensor, co
 
 
 GEMM_MODES = {"store": 0, "residual": 1, "swiglu": 2}
-_GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters zero
+_GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters and sums zero
 _GEMM_WS_RETIRED: list = []  # outgrown workspaces, kept alive for CUDA graphs that captured them
 
 
