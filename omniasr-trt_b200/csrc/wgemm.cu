@@ -106,55 +106,77 @@ OMNI_DEV void stage_tokens(const GemmArgs& a, int m, TokenPlace* place) {
 template <int NT, int MODE>
 OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&acc)[NT], float* xch, int bar) {
   if (MODE == kGemmRope) {
-    // Feature f = tile * 128 + row is head dim d of head h of section q / k / v (128 divides the head_dim, so a
-    // rotation pair (2j, 2j + 1) never straddles two tiles: its partner is the neighbouring lane). Each product is
-    // rounded to bf16 first, as the GEMM's output would be, then rotated in fp32 with the non-contracting products
-    // of rope_kv.cu (omniasr_trt/modeling.py:301-306). The tokens' places come from shared memory (`xch`, staged by
-    // stage_tokens); their cos/sin pairs are fetched eight tokens at a time ahead of the stores.
+    // The tile's 128 features are dims d0..d0+127 of one head h of section q / k / v (128 divides the head_dim);
+    // thread `row` holds dim d0 + row, so a rotation pair (2j, 2j + 1) is two neighbouring lanes (one shuffle).
+    // Each product is rounded to bf16 first, as the GEMM's output would be, then rotated in fp32 with the
+    // non-contracting products of rope_kv.cu (omniasr_trt/modeling.py:301-306); cos/sin pairs are fetched for a
+    // batch of tokens at a time ahead of their use. The rotated tile is staged as bf16 [NT][128] in shared memory after
+    // the tokens' places (staged once per CTA by stage_tokens), then written as 16-byte runs of one token's dims:
+    // q always (zero for a position outside the table), k only with a rotation and a cache slot, v with a slot.
     const RopeArgs& r = a.rope;
     const TokenPlace* place = reinterpret_cast<const TokenPlace*>(xch);
-    const int f = tile * BM + row;
+    __nv_bfloat16* stage =
+        reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(xch) + kGemmMaxRows * sizeof(TokenPlace));
     const int per = r.heads * a.head_dim;
-    const int part = f / per, h = (f - part * per) / a.head_dim, d = f - part * per - h * a.head_dim;
-    const bool odd = d & 1;
-    const float* cs_base = r.cs + (d & ~1);
-    __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(r.q_out) + (int64_t)h * a.head_dim + d;
-    const int64_t head_off = (int64_t)h * r.s_kh + d;
+    const int f0 = tile * BM, part = f0 / per, h = (f0 - part * per) / a.head_dim;
+    const int d0 = f0 - part * per - h * a.head_dim;
+    const bool odd = row & 1;
+    const float* cs_base = r.cs + ((d0 + row) & ~1);
+    constexpr int HALF = NT == 64 ? 16 : NT / 2;  // tokens per batch of cos/sin loads (64: a quarter, for registers)
 #pragma unroll
-    for (int m0 = 0; m0 < NT; m0 += 8) {
-      float2 cs[8];
-      int64_t coff[8];
-      bool rot[8];
+    for (int m0 = 0; m0 < NT; m0 += HALF) {
+      float2 cs[HALF];
+      bool rot[HALF];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < HALF; ++j) {
         const int m = m0 + j;
         const int64_t so = m < a.rows && part < 2 ? place[m].cs_off : -1;
-        coff[j] = m < a.rows ? place[m].cache_off : -1;
         rot[j] = so >= 0;
         cs[j] = rot[j] ? __ldg(reinterpret_cast<const float2*>(cs_base + so)) : make_float2(0.f, 0.f);
-        if (so < 0) coff[j] = part < 2 ? -1 : coff[j];  // no k without a rotation (v needs none)
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < HALF; ++j) {
         const int m = m0 + j;
         const float x = bf16r(acc[m]);
         const float other = __shfl_xor_sync(0xffffffffu, x, 1);
-        if (m >= a.rows || f >= a.n) continue;
-        if (part == 2) {
-          if (coff[j] >= 0) reinterpret_cast<__nv_bfloat16*>(r.v_cache)[coff[j] + head_off] = __float2bfloat16_rn(x);
-          continue;
-        }
         const float re = odd ? other : x, im = odd ? x : other;
-        const float y = !rot[j] ? 0.f
-                        : odd   ? __fadd_rn(__fmul_rn(re, cs[j].y), __fmul_rn(im, cs[j].x))
-                                : __fsub_rn(__fmul_rn(re, cs[j].x), __fmul_rn(im, cs[j].y));
-        if (part == 0) {
-          q_out[(int64_t)m * r.heads * a.head_dim] = __float2bfloat16_rn(y);  // zero for a position outside the table
-        } else if (coff[j] >= 0) {
-          reinterpret_cast<__nv_bfloat16*>(r.k_cache)[coff[j] + head_off] = __float2bfloat16_rn(y);
-        }
+        const float y = part == 2 ? x
+                        : !rot[j] ? 0.f
+                        : odd     ? __fadd_rn(__fmul_rn(re, cs[j].y), __fmul_rn(im, cs[j].x))
+                                  : __fsub_rn(__fmul_rn(re, cs[j].x), __fmul_rn(im, cs[j].y));
+        stage[m * BM + row] = __float2bfloat16_rn(y);
       }
     }
+    named_sync(bar, 128);
+    __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(r.q_out);
+    __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(part == 1 ? r.k_cache : r.v_cache);
+    const bool vec = part == 0 ? (reinterpret_cast<uintptr_t>(q_out) & 15) == 0
+                               : (reinterpret_cast<uintptr_t>(cache) & 15) == 0 &&
+                                     ((r.s_kb | r.s_kh | r.s_ks) & 7) == 0;
+    constexpr int RUNS = BM / 8;
+    constexpr int MAXK = (NT * RUNS + 127) / 128;
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+      const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
+      if (c >= a.rows * RUNS) break;
+      __nv_bfloat16* dst;
+      if (part == 0) {
+        dst = q_out + (int64_t)m * per + (int64_t)h * a.head_dim + d0 + j0;
+      } else {
+        const int64_t co = place[m].cache_off;
+        if (co < 0 || (part == 1 && place[m].cs_off < 0)) continue;
+        dst = cache + co + (int64_t)h * r.s_kh + d0 + j0;
+      }
+      const uint4 v = *reinterpret_cast<const uint4*>(stage + m * BM + j0);
+      if (vec) {
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const __nv_bfloat16* v8 = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = v8[q];
+      }
+    }
+    named_sync(bar, 128);  // the stage is free again
     return;
   }
   // Store / residual / SwiGLU: the tile goes through shared memory (`xch`, [NT][128] fp32, thread `row` writes
@@ -171,7 +193,8 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
   const int64_t col0 = (int64_t)tile * WIDTH;
   const int cols = (int)min((int64_t)WIDTH, (int64_t)a.n - col0);
   const bool vec_y = (a.ld_y & 7) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
-  const bool vec_r = MODE != kGemmResidual || ((a.ld_res & 7) == 0 && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0);
+  const bool vec_r =
+      MODE != kGemmResidual || ((a.ld_res & 7) == 0 && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0);
   const int runs = a.rows * RUNS;
   uint4 res[MAXK];
   if (MODE == kGemmResidual) {
@@ -298,7 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int c = (int)(u % a.chunks);
     unsigned char* st = smem + (i % STAGES) * L::STAGE;
 #pragma unroll
-    for (int j = 0; j < KB; ++j) tma_load_2d(st + W_BYTES + j * L::X_BOX, &xmap, c * BKU + j * BK, 0, &full[i % STAGES]);
+    for (int j = 0; j < KB; ++j)
+      tma_load_2d(st + W_BYTES + j * L::X_BOX, &xmap, c * BKU + j * BK, 0, &full[i % STAGES]);
   };
   // The weights do not depend on the kernel before: the first stages' weight boxes are requested before the
   // dependency wait, so their latency overlaps that kernel's tail.
