@@ -201,7 +201,9 @@ int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, i
  * workspace (omniasr_decode_gemm_workspace() bytes, 16-byte aligned) holds per-tile arrival counters and fp32 sums
  * of the tiles split between CTAs; all of it must be ZERO when a call starts, and every call that completes leaves
  * it zero again, so a caller zeroes a workspace once and keeps it (one per stream: calls sharing a workspace must
- * not overlap on the GPU; after status bit 2 it may be left non-zero and is to be zeroed or replaced). Replaces the decoder step's weight GEMMs
+ * not overlap on the GPU; after status bit 2 it may be left non-zero and is to be zeroed or replaced). The kernel
+ * is launched as a programmatic dependent and requests its first weight tiles before waiting for the kernel before
+ * it, so w must not be written by the kernel launched just before on the same stream (x and the residual may be). Replaces the decoder step's weight GEMMs
  * of omniasr_trt/decode.py:201-205 / spec.py:100-107 (`qkv = norm(h) @ qkv_w.t()`, `torch.addmm(h, o, out_w.t())`,
  * `(norm(h) @ gi_w.t()).chunk(2)` + `inner * F.silu(gate)`, `torch.addmm(h, ..., ffo_w.t())`), which the reference
  * leaves to cuBLAS. */
@@ -218,7 +220,8 @@ int omniasr_decode_gemm(const void* x, int64_t x_stride, int rows, const void* w
  * be, and then handled as omniasr_rope_kv() handles a qkv row -- q rotated into q_out [rows, heads, dim], k rotated
  * and v as it is written into the caches at cache row slots[m] (or m) and position cache_pos[m] (or pos[m]) -- without
  * qkv ever reaching memory. Arguments as omniasr_decode_gemm() and omniasr_rope_kv(); the workspace is sized by
- * omniasr_decode_gemm_workspace(rows, 3 * heads * dim, k, OMNIASR_GEMM_STORE) and follows the same counter rule.
+ * omniasr_decode_gemm_workspace(rows, 3 * heads * dim, k, OMNIASR_GEMM_STORE) and follows the same counter rule;
+ * w likewise must not be written by the kernel launched just before on the same stream.
  * dim must be a multiple of 128. Replaces `qkv = norm(h) @ qkv_w.t()` followed by kernels.rope_kv
  * (omniasr_trt/decode.py:201-203, spec.py:100-101). */
 int omniasr_decode_gemm_rope(const void* x, int64_t x_stride, int rows, const void* w, int64_t w_stride, int k,

@@ -21,6 +21,8 @@
 // SwiGLU: the gate and inner rows of the same 64 outputs are two 64-row boxes of one 128-row tile (no weight copy),
 // so the epilogue forms inner * silu(gate) within the tile.
 
+#include <algorithm>
+#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include "attention.cuh"
@@ -50,11 +52,16 @@ constexpr int KB = OMNI_WGEMM_KB;  // boxes per stage along K: each weight row g
 constexpr int BKU = BK * KB;       // K per unit (chunk)
 constexpr int W_BOX = BM * BK * 2;
 constexpr int W_BYTES = KB * W_BOX;
+// The first stages' weight boxes are requested before the dependency wait (the weights must not be written by the
+// kernel launched just before on the same stream), and the next kernel may launch once every load is issued.
 #ifndef OMNI_WGEMM_PREFETCH
-#define OMNI_WGEMM_PREFETCH 0
+#define OMNI_WGEMM_PREFETCH 1
 #endif
 #ifndef OMNI_WGEMM_EARLY_TRIGGER
-#define OMNI_WGEMM_EARLY_TRIGGER 0
+#define OMNI_WGEMM_EARLY_TRIGGER 1
+#endif
+#ifndef OMNI_WGEMM_CLUSTER
+#define OMNI_WGEMM_CLUSTER 1  // the per-tile cluster mode of launch_decode_gemm
 #endif
 #ifndef OMNI_WGEMM_STAGES
 #define OMNI_WGEMM_STAGES (8 / OMNI_WGEMM_KB)
@@ -98,6 +105,73 @@ OMNI_DEV void stage_tokens(const GemmArgs& a, int m, TokenPlace* place) {
   if (!pos_ok || !dst_ok) raise_status(a.status, kStatusIndex);
   place[m].cs_off = pos_ok ? p * a.head_dim : -1;
   place[m].cache_off = dst_ok ? crow * r.s_kb + cp * r.s_ks : -1;
+}
+
+// Writes out token rows [m_lo, m_hi) of a finished tile held in `xch` ([NT][128] fp32: row m, column = the weight
+// row of the tile) -- each thread 16-byte runs of 8 outputs of one token row, one vector store (and one vector
+// residual load, all of a thread's loads issued before its first store, since y may be the residual) per 8 outputs.
+// SwiGLU: columns 0..63 are the gate and 64..127 the inner products of outputs tile * 64 + c, each rounded to bf16
+// before inner * silu(gate). The 128 threads call this together; it ends with the named barrier `bar`.
+template <int NT, int MODE>
+OMNI_DEV void finish_rows(const GemmArgs& a, int tile, int row, const float* xch, int m_lo, int m_hi, int bar) {
+  constexpr int WIDTH = MODE == kGemmSwiglu ? 64 : BM;  // outputs of one tile
+  constexpr int RUNS = WIDTH / 8;                       // 16-byte runs per token row
+  constexpr int MAXK = (NT * RUNS + 127) / 128;         // runs per thread
+  const int64_t col0 = (int64_t)tile * WIDTH;
+  const int cols = (int)min((int64_t)WIDTH, (int64_t)a.n - col0);
+  const bool vec_y = (a.ld_y & 7) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  const bool vec_r =
+      MODE != kGemmResidual || ((a.ld_res & 7) == 0 && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0);
+  const int runs = (m_hi - m_lo) * RUNS;
+#pragma unroll 1  // compact: see the epilogue's finish below
+  for (int k = 0; k < MAXK; ++k) {
+    const int c = row + 128 * k, m = m_lo + c / RUNS, j0 = (c % RUNS) * 8;
+    if (c >= runs) break;
+    uint4 res = make_uint4(0u, 0u, 0u, 0u);
+    if (MODE == kGemmResidual) {
+      const __nv_bfloat16* rsrc = a.residual + (int64_t)m * a.ld_res + col0 + j0;
+      if (vec_r && j0 + 8 <= cols) {
+        res = *reinterpret_cast<const uint4*>(rsrc);
+      } else {
+        __nv_bfloat16* r8 = reinterpret_cast<__nv_bfloat16*>(&res);
+        for (int q = 0; q < 8; ++q)
+          if (j0 + q < cols) r8[q] = rsrc[q];
+      }
+    }
+    const float4* src = reinterpret_cast<const float4*>(xch + m * BM + j0);
+    float v[8];
+    if (MODE == kGemmSwiglu) {
+      const float4 g0 = src[0], g1 = src[1], u0 = src[16], u1 = src[17];  // inner products: 64 columns on
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float gq = bf16r(g[q]);
+        const float sq = bf16r(gq / (1.f + __expf(-gq)));
+        v[q] = bf16r(u[q]) * sq;
+      }
+    } else {
+      const float4 v0 = src[0], v1 = src[1];
+      v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w, v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
+      if (MODE == kGemmResidual) {
+        const __nv_bfloat16* r8 = reinterpret_cast<const __nv_bfloat16*>(&res);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] += __bfloat162float(r8[q]);
+      }
+    }
+    uint4 out;
+    __nv_bfloat16* o8 = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o8[q] = __float2bfloat16_rn(v[q]);
+    __nv_bfloat16* dst = a.y + (int64_t)m * a.ld_y + col0 + j0;
+    if (vec_y && j0 + 8 <= cols) {
+      *reinterpret_cast<uint4*>(dst) = out;
+    } else {
+      for (int q = 0; q < 8; ++q)
+        if (j0 + q < cols) dst[q] = o8[q];
+    }
+  }
+  named_sync(bar, 128);  // xch free again
 }
 
 // The epilogue of one finished weight tile: thread `row` (0..127) holds acc[m] of token m for weight row
@@ -155,7 +229,7 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
                                      ((r.s_kb | r.s_kh | r.s_ks) & 7) == 0;
     constexpr int RUNS = BM / 8;
     constexpr int MAXK = (NT * RUNS + 127) / 128;
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < MAXK; ++k) {
       const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
       if (c >= a.rows * RUNS) break;
@@ -180,80 +254,11 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
     return;
   }
   // Store / residual / SwiGLU: the tile goes through shared memory (`xch`, [NT][128] fp32, thread `row` writes
-  // column `row`), then each thread writes 16-byte runs of 8 outputs of one token row -- one vector store (and one
-  // vector residual load, all of a thread's loads issued before its first store, since y may be the residual) per 8
-  // outputs instead of one 2-byte store per output. SwiGLU: columns 0..63 are the gate and 64..127 the inner
-  // products of outputs tile * 64 + c, each rounded to bf16 before inner * silu(gate).
+  // column `row`), then finish_rows writes it out.
 #pragma unroll
   for (int m = 0; m < NT; ++m) xch[m * BM + row] = acc[m];
   named_sync(bar, 128);
-  constexpr int WIDTH = MODE == kGemmSwiglu ? 64 : BM;  // outputs of one tile
-  constexpr int RUNS = WIDTH / 8;                       // 16-byte runs per token row
-  constexpr int MAXK = (NT * RUNS + 127) / 128;         // runs per thread
-  const int64_t col0 = (int64_t)tile * WIDTH;
-  const int cols = (int)min((int64_t)WIDTH, (int64_t)a.n - col0);
-  const bool vec_y = (a.ld_y & 7) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
-  const bool vec_r =
-      MODE != kGemmResidual || ((a.ld_res & 7) == 0 && (reinterpret_cast<uintptr_t>(a.residual) & 15) == 0);
-  const int runs = a.rows * RUNS;
-  uint4 res[MAXK];
-  if (MODE == kGemmResidual) {
-#pragma unroll
-    for (int k = 0; k < MAXK; ++k) {
-      const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
-      res[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (c < runs) {
-        const __nv_bfloat16* src = a.residual + (int64_t)m * a.ld_res + col0 + j0;
-        if (vec_r && j0 + 8 <= cols) {
-          res[k] = *reinterpret_cast<const uint4*>(src);
-        } else {
-          __nv_bfloat16* r8 = reinterpret_cast<__nv_bfloat16*>(&res[k]);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (j0 + q < cols) r8[q] = src[q];
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < MAXK; ++k) {
-    const int c = row + 128 * k, m = c / RUNS, j0 = (c % RUNS) * 8;
-    if (c >= runs) break;
-    const float4* src = reinterpret_cast<const float4*>(xch + m * BM + j0);
-    float v[8];
-    if (MODE == kGemmSwiglu) {
-      const float4 g0 = src[0], g1 = src[1], u0 = src[16], u1 = src[17];  // inner products: 64 columns on
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float gq = bf16r(g[q]);
-        const float sq = bf16r(gq / (1.f + __expf(-gq)));
-        v[q] = bf16r(u[q]) * sq;
-      }
-    } else {
-      const float4 v0 = src[0], v1 = src[1];
-      v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w, v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
-      if (MODE == kGemmResidual) {
-        const __nv_bfloat16* r8 = reinterpret_cast<const __nv_bfloat16*>(&res[k]);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] += __bfloat162float(r8[q]);
-      }
-    }
-    uint4 out;
-    __nv_bfloat16* o8 = reinterpret_cast<__nv_bfloat16*>(&out);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) o8[q] = __float2bfloat16_rn(v[q]);
-    __nv_bfloat16* dst = a.y + (int64_t)m * a.ld_y + col0 + j0;
-    if (vec_y && j0 + 8 <= cols) {
-      *reinterpret_cast<uint4*>(dst) = out;
-    } else {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (j0 + q < cols) dst[q] = o8[q];
-    }
-  }
-  named_sync(bar, 128);  // xch free again
+  finish_rows<NT, MODE>(a, tile, row, xch, 0, a.rows, bar);
 }
 
 template <int NT, int MODE>
@@ -273,9 +278,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) OMNI_WG_EVENT(a, 0);
   const int64_t total = (int64_t)a.tiles * a.chunks;
-  const int64_t u0 = (int64_t)blockIdx.x * a.per;
-  const int64_t u1 = min(total, u0 + a.per);
-  if (u0 >= u1) return;  // uniform over the CTA
+  // Stream-K: one contiguous range of `per` units per CTA. Cluster mode (a.cluster = S > 1): cluster i (CTAs
+  // S * i .. S * i + S - 1, rank = blockIdx.x % S) owns tile i, each CTA a contiguous 1/S of its chunks; the host
+  // chooses it only when every CTA gets at least one chunk, so no CTA of a cluster leaves early.
+  const int S = a.cluster;
+  const int64_t u0 = S > 1 ? (int64_t)(blockIdx.x / S) * a.chunks + (blockIdx.x % S) * a.chunks / S
+                           : (int64_t)blockIdx.x * a.per;
+  const int64_t u1 = S > 1 ? (int64_t)(blockIdx.x / S) * a.chunks + (blockIdx.x % S + 1) * a.chunks / S
+                           : min(total, u0 + a.per);
+  if (u0 >= u1) return;  // uniform over the CTA (never in cluster mode)
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -413,6 +424,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t seg_end = min(u1, (int64_t)(t + 1) * a.chunks);  // exclusive
       const bool whole = c0 == 0 && seg_end == (int64_t)(t + 1) * a.chunks;
       const int buf = seg & 1;
+      if (S > 1) {
+        // Cluster mode: the CTA's one range; its partial goes to the (now idle) stage area, [NT][128] fp32, for the
+        // cluster's reduction after the role loops.
+        if (!mbar_wait(&acc_full[buf], (seg >> 1) & 1)) abort_flag = 1;
+        tc_fence_after();
+        __syncwarp();
+        float acc[NT];
+#pragma unroll
+        for (int c = 0; c < NT; c += 16) tmem_ld16(tbase + lane_off + buf * NT + c, acc + c);
+        tc_fence_before();
+        mbar_arrive(&acc_free[buf]);
+        float* part = reinterpret_cast<float*>(smem);
+#pragma unroll
+        for (int m = 0; m < NT; ++m) part[m * BM + row] = acc[m];
+        u = seg_end;
+        continue;
+      }
       // A split tile's contributors are CTAs b0..b1; each leaves its fp32 partial in its own slot and the tile is
       // summed in one fixed order, p[b1] + p[b1 - 1] + ... + p[b0], whoever finishes it, so results do not depend
       // on timing. The contributor that begins the tile (b0: the last range of its CTA, while the others met the
@@ -473,16 +501,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < NT; c += 16) tmem_ld16(tbase + lane_off + buf * NT + c, acc + c);
       tc_fence_before();
       mbar_arrive(&acc_free[buf]);
-      if (whole) {
-        finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
-      } else if (early) {
+      // Whole tiles, early finishes and last arrivals all end in the one finish_tile below: the kernel's code stays
+      // small, and code size matters here (the epilogue runs once or twice per call, and a larger body slowed the
+      // weight stream of the other warps as well).
+      bool finish = whole;
+      if (!whole && early) {
 #pragma unroll
         for (int m = 0; m < NT; ++m) acc[m] = others[m] + acc[m];
-        if (tid == 64) OMNI_WG_EVENT(a, 12);
-        finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
-        if (tid == 64) OMNI_WG_EVENT(a, 13);
-        if (row == 0) a.counters[t] = 0;  // zero again for the next call
-      } else {
+        finish = true;
+      } else if (!whole) {
         float4* dst = const_cast<float4*>(slot_of(me));
 #pragma unroll
         for (int m = 0; m < NT; m += 4) dst[(m / 4) * BM] = make_float4(acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
@@ -491,7 +518,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (row == 0) *last_flag = atomicAdd(&a.counters[t], 1) == b1 - b0;
         named_sync(2, 128);
         if (tid == 64) OMNI_WG_EVENT(a, 14);
-        if (*last_flag) {
+        finish = *last_flag;
+        if (finish) {
           __threadfence();
           // Two slots per round trip, summed in the fixed order.
           for (int b = b1; b >= b0; b -= 2) {
@@ -515,10 +543,13 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
-          if (tid == 64) OMNI_WG_EVENT(a, 15);
-          finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
-          if (row == 0) a.counters[t] = 0;  // zero again for the next call
         }
+      }
+      if (finish) {
+        if (tid == 64) OMNI_WG_EVENT(a, 12);
+        finish_tile<NT, MODE>(a, t, row, acc, xch, 1);
+        if (tid == 64) OMNI_WG_EVENT(a, 13);
+        if (!whole && row == 0) a.counters[t] = 0;  // zero again for the next call
       }
       u = seg_end;
       if (abort_flag) break;
@@ -537,6 +568,63 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (abort_flag && tid == 0) {
     // Let the latest load of every stage land before the shared memory goes away.
     for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+  }
+  if (S > 1) {
+    // Cluster mode: the S partials of the tile are summed through distributed shared memory, rank S - 1 first
+    // (a fixed order), each CTA for its share of the token rows, which it then writes out.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    if (tid == 64) OMNI_WG_EVENT(a, 11);
+    cluster.sync();  // every partial of the cluster in place
+    if (tid == 64) OMNI_WG_EVENT(a, 12);
+    if (warp >= 2) {
+      const int row = 32 * (warp & 3) + lane;
+      const int q = (int)cluster.block_rank();
+      const int m_lo = q * a.rows / S, m_hi = (q + 1) * a.rows / S;
+      float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
+      // Thread = (one of 4 token rows, 4 consecutive weight rows); two token rows per pass, every rank's float4 of
+      // both requested before any is summed, so a pass costs one distributed-shared-memory round trip.
+      constexpr int MAXS = 8;
+      const int g = row & 31, mo = row >> 5;
+      const float4* src[MAXS];
+#pragma unroll
+      for (int j = 0; j < MAXS; ++j)
+        src[j] = reinterpret_cast<const float4*>(cluster.map_shared_rank(reinterpret_cast<float*>(smem), j < S ? j : 0));
+      for (int m0 = m_lo + mo; m0 < m_hi; m0 += 8) {
+        const int m1 = m0 + 4;
+        const bool two = m1 < m_hi;
+        float4 v0[MAXS], v1[MAXS];
+#pragma unroll
+        for (int j = 0; j < MAXS; ++j) {
+          if (j < S) {
+            v0[j] = src[j][m0 * (BM / 4) + g];
+            if (two) v1[j] = src[j][m1 * (BM / 4) + g];
+          }
+        }
+        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+        bool first = true;
+#pragma unroll
+        for (int j = MAXS - 1; j >= 0; --j) {  // rank S - 1 first: a fixed order
+          if (j < S) {
+            if (first) {
+              s0 = v0[j], s1 = v1[j];
+            } else {
+              s0.x += v0[j].x, s0.y += v0[j].y, s0.z += v0[j].z, s0.w += v0[j].w;
+              s1.x += v1[j].x, s1.y += v1[j].y, s1.z += v1[j].z, s1.w += v1[j].w;
+            }
+            first = false;
+          }
+        }
+        reinterpret_cast<float4*>(xch)[m0 * (BM / 4) + g] = s0;
+        if (two) reinterpret_cast<float4*>(xch)[m1 * (BM / 4) + g] = s1;
+      }
+      named_sync(1, 128);
+      if (tid == 64) OMNI_WG_EVENT(a, 13);
+      finish_rows<NT, MODE>(a, (int)(u0 / a.chunks), row, xch, m_lo, m_hi, 1);
+      if (tid == 64) OMNI_WG_EVENT(a, 14);
+    }
+    cluster.sync();  // no CTA leaves while the others read its partial
+    if (tid == 64) OMNI_WG_EVENT(a, 15);
   }
   tc_fence_before();
   __syncthreads();
@@ -577,8 +665,24 @@ cudaError_t launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArg
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_dependent(wgemm_kernel<NT, MODE>, dim3((unsigned)a.grid), dim3(THREADS), (size_t)L::BYTES, stream, wm,
-                          xm, a);
+  if (a.cluster <= 1)
+    return launch_dependent(wgemm_kernel<NT, MODE>, dim3((unsigned)a.grid), dim3(THREADS), (size_t)L::BYTES, stream,
+                            wm, xm, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = (size_t)L::BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)a.cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, wgemm_kernel<NT, MODE>, wm, xm, a);
 }
 
 template <int NT>
@@ -627,10 +731,24 @@ cudaError_t launch_decode_gemm(const void* x, int64_t ldx, const void* w, int64_
   a.tiles = gemm_tiles(a.n, a.mode);
   a.chunks = (a.k + BKU - 1) / BKU;
   const int64_t total = (int64_t)a.tiles * a.chunks;
-  int grid = device_sm_count();
+  const int sms = device_sm_count();
+  int grid = sms;
   if (grid > total) grid = (int)total;
   a.per = (total + grid - 1) / grid;
   a.grid = (int)((total + a.per - 1) / a.per);
+  // Few, long tiles (the 4096-wide projections: 32 tiles on 148 SMs): stream-K would cut each tile between four or
+  // five CTAs that all finish at the end of the call, leaving a chain of global round trips to whichever is last.
+  // Instead a cluster of S CTAs takes each tile and reduces it through distributed shared memory -- when that still
+  // keeps three quarters of the SMs streaming.
+  a.cluster = 1;
+  if (OMNI_WGEMM_CLUSTER && a.mode != kGemmRope) {
+    int S = std::min(8, sms / a.tiles);
+    while (S > 1 && a.chunks < S) --S;
+    if (S > 1 && 4 * a.tiles * S >= 3 * sms) {
+      a.cluster = S;
+      a.grid = a.tiles * S;
+    }
+  }
   const size_t cbytes = gemm_counter_bytes(a.n, a.mode);
   if (workspace_bytes < cbytes + (size_t)a.grid * 2 * BM * nt * sizeof(float)) return cudaErrorInvalidValue;
   a.counters = static_cast<int*>(workspace);

@@ -27,6 +27,7 @@ struct GemmArgs {
   float* part;    // [grid, 2, NT / 4, 128, 4] fp32 partials of weight tiles split between CTAs
   int* counters;  // [tiles] arrivals on split tiles: zero before and after a call
   int tiles, chunks, grid;
+  int cluster;  // 1: stream-K; S > 1: a cluster of S CTAs per tile, reduced through distributed shared memory
   int64_t per;  // (tile, chunk) units per CTA
   int* status;
   RopeArgs rope;  // kGemmRope: positions, cos/sin table, q output, caches (rope.qkv unused)

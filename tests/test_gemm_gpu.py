@@ -50,7 +50,7 @@ def test_residual(rows, n, k):
 
 
 @pytest.mark.parametrize("rows", [8, 40])
-@pytest.mark.parametrize("f,k", [(11008, 4096), (100, 256)])
+@pytest.mark.parametrize("f,k", [(11008, 4096), (2048, 4096), (100, 256)])
 def test_swiglu(rows, f, k):
     x, w = data(rows, f, k, rows + f + 2, wrows=2 * f)
     y = K().decode_gemm(x, w, "swiglu")
@@ -88,10 +88,12 @@ def test_shapes_in_turn_share_one_workspace():
 
 @pytest.mark.parametrize("rows,n,k,mode", [(40, 12288, 4096, "store"), (40, 4096, 4096, "residual"),
                                            (40, 4096, 11008, "residual"), (40, 11008, 4096, "swiglu"),
+                                           (40, 2048, 4096, "swiglu"), (1, 4096, 4096, "store"),
                                            (8, 10288, 4096, "store")])
 def test_repeated_calls_give_the_same_bits(rows, n, k, mode):
-    """Tiles split between CTAs are summed in one fixed order whichever CTA finishes them, so repeated calls on the
-    same inputs (shapes whose tiles have two to five contributors) give identical bits."""
+    """Tiles split between CTAs are summed in one fixed order whichever CTA finishes them (stream-K) and in rank
+    order within a tile's cluster (the 4096-wide and 2048-wide shapes), so repeated calls on the same inputs give
+    identical bits."""
     x, w = data(rows, n, k, 3 * rows + n, wrows=2 * n if mode == "swiglu" else None)
     h = torch.randn(rows, n, device="cuda").to(torch.bfloat16) if mode == "residual" else None
     first = K().decode_gemm(x, w, mode, residual=h).clone()
