@@ -67,6 +67,7 @@ constexpr int W_BYTES = KB * W_BOX;
 #define OMNI_WGEMM_STAGES (8 / OMNI_WGEMM_KB)
 #endif
 constexpr int STAGES = OMNI_WGEMM_STAGES;
+constexpr int kMaxCluster = 4;  // CTAs per tile in cluster mode (the reduction is unrolled over this many ranks)
 constexpr int THREADS = 192;
 
 template <int NT>
@@ -584,7 +585,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float* xch = reinterpret_cast<float*>(smem + L::XCH_OFF);
       // Thread = (one of 4 token rows, 4 consecutive weight rows); two token rows per pass, every rank's float4 of
       // both requested before any is summed, so a pass costs one distributed-shared-memory round trip.
-      constexpr int MAXS = 8;
+      constexpr int MAXS = kMaxCluster;
       const int g = row & 31, mo = row >> 5;
       const float4* src[MAXS];
 #pragma unroll
@@ -742,7 +743,7 @@ cudaError_t launch_decode_gemm(const void* x, int64_t ldx, const void* w, int64_
   // keeps three quarters of the SMs streaming.
   a.cluster = 1;
   if (OMNI_WGEMM_CLUSTER && a.mode != kGemmRope) {
-    int S = std::min(8, sms / a.tiles);
+    int S = std::min(kMaxCluster, sms / a.tiles);
     while (S > 1 && a.chunks < S) --S;
     if (S > 1 && 4 * a.tiles * S >= 3 * sms) {
       a.cluster = S;
