@@ -198,10 +198,10 @@ int omniasr_accept(const int64_t* tokens, const int64_t* argmax, int32_t* out, i
  *   OMNIASR_GEMM_RESIDUAL  y[m, j] = residual[m, j] + x[m, :] . w[j, :]          (torch.addmm(residual, x, w.t()))
  *   OMNIASR_GEMM_SWIGLU    w = [gate; inner] (2n rows): y[m, j] = inner * silu(gate), each rounded to bf16 first
  * x [rows, k] and w row-major with element row strides (16-byte aligned rows); y / residual [rows, n]. The
- * workspace (omniasr_decode_gemm_workspace() bytes, 16-byte aligned) holds per-tile arrival counters and fp32 sums
- * of the tiles split between CTAs; all of it must be ZERO when a call starts, and every call that completes leaves
- * it zero again, so a caller zeroes a workspace once and keeps it (one per stream: calls sharing a workspace must
- * not overlap on the GPU; after status bit 2 it may be left non-zero and is to be zeroed or replaced). The kernel
+ * workspace (omniasr_decode_gemm_workspace() bytes, 16-byte aligned) starts with per-tile arrival counters that
+ * must be ZERO when a call starts (the partial tiles after them need no initial value); every call that completes
+ * leaves them zero again, so a caller zeroes a workspace once and keeps it (one per stream: calls sharing a
+ * workspace must not overlap on the GPU; after status bit 2 they may be left non-zero: zero or replace it). The kernel
  * is launched as a programmatic dependent and requests its first weight tiles before waiting for the kernel before
  * it, so w must not be written by the kernel launched just before on the same stream (x and the residual may be). Replaces the decoder step's weight GEMMs
  * of omniasr_trt/decode.py:201-205 / spec.py:100-107 (`qkv = norm(h) @ qkv_w.t()`, `torch.addmm(h, o, out_w.t())`,

@@ -64,7 +64,7 @@ def status_word(device: torch.device | int | None = None) -> torch.Tensor:
 
 def read_status(device=None, clear: bool = True) -> int:
     """Synchronises, returns the status word and clears it. After a wait that gave up (bit 2) the unit counters of
-    the decode / draft workspaces and the split-tile counters and sums of the GEMM workspaces may be left non-zero,
+    the decode / draft workspaces and the split-tile counters of the GEMM workspaces may be left non-zero,
     so those workspaces are dropped (the next call zeroes a new one)."""
     word = status_word(device)
     value = int(word.item())
@@ -391,7 +391,7 @@ def beam_select(logp: torch.Tensor, score: torch.Tensor, ended: torch.Tensor, co
 
 
 GEMM_MODES = {"store": 0, "residual": 1, "swiglu": 2}
-_GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters and sums zero
+_GEMM_WS: dict = {}  # (device, stream) -> zero-initialised workspace; the kernel leaves its counters zero
 _GEMM_WS_RETIRED: list = []  # outgrown workspaces, kept alive for CUDA graphs that captured them
 
 
