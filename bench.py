@@ -1177,9 +1177,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 STEP_B, STEP_W, STEP_STEPS, STEP_SYNC = 8, 1500, 256, 8
 
 
-def reference_modules(ours: bool):
+def reference_modules(ours: bool, gemm: bool = False):
     """The reference package (Wataru-Nakata/omniasr-trt) from baseline/_ref, with this library's kernels in place of
-    its ``omniasr_trt.kernels`` when ``ours`` (the drop-in); (modules, None) or (None, why not)."""
+    its ``omniasr_trt.kernels`` when ``ours`` (the drop-in; with ``gemm`` also the step's weight products);
+    (modules, None) or (None, why not)."""
     ref = ROOT / "baseline" / "_ref"
     if not (ref / "omniasr_trt" / "spec.py").exists():
         return None, "the reference package is not installed in baseline/_ref"
@@ -1188,7 +1189,7 @@ def reference_modules(ours: bool):
     if ours:
         from omniasr_b200 import dropin
 
-        dropin.install()
+        dropin.install(gemm=gemm)
     from omniasr_trt import decode, llm, modeling, spec
 
     return {"decode": decode, "llm": llm, "modeling": modeling, "spec": spec}, None
@@ -1274,7 +1275,7 @@ def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict |
     impl = "b200" if ours else "reference"
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    mods, why = reference_modules(ours)
+    mods, why = reference_modules(ours, gemm=ours and args.step_gemm == "b200")
     if mods is None:
         return {"impl": impl, "unavailable": why} if rank == 0 else None
     torch.manual_seed(0)
@@ -1337,7 +1338,8 @@ def run_step(args, rank: int, world: int, local_rank: int, ours: bool) -> dict |
         "config": {"workload": "BASELINE config 4: the reference's SpecDecoder (draft_tokens 4, batch 8 per GPU, "
                                "sync_every 8) on a 12-layer d4096 32x128 SwiGLU-11008 vocab-10288 decoder; prefill "
                                "of 8 x 1500 frames, then 256 steps",
-                   "kernels": "omniasr_b200 (drop-in: attention, RoPE/append, prefill, propose, accept)" if ours
+                   "kernels": ("omniasr_b200 (drop-in: attention, RoPE/append, prefill, propose, accept"
+                               + (", the step's weight products)" if args.step_gemm == "b200" else ")")) if ours
                    else "the reference's Triton kernels",
                    "global_batch": STEP_B * world, "prefill_ms": round(pre_ms, 3), "timing": "median of 3 runs",
                    "prefill_frames_per_s": round(world * STEP_B * STEP_W / (pre_ms * 1e-3), 1),
@@ -1400,6 +1402,9 @@ def main():
     p.add_argument("--tokens-out", default=None, help="step workload: save the generated tokens (.npy)")
     p.add_argument("--decode-steps", type=int, default=STEP_STEPS, help="step workload: decoder steps per run")
     p.add_argument("--dtype", choices=["bf16", "f32"], default="bf16", help="step workload: model dtype")
+    p.add_argument("--step-gemm", choices=["cublas", "b200"], default="cublas",
+                   help="step workload, this library's arm: the decoder's weight products on cuBLAS (as the reference "
+                        "runs them) or on this library's decode GEMM (dropin.install(gemm=True))")
     p.add_argument("--heads", type=int, default=H, help="attention workloads: heads (heads x head_dim = 4096)")
     p.add_argument("--head-dim", type=int, default=D,
                    help="attention workloads: head_dim; 512 with 8 heads is the shipped model's geometry")

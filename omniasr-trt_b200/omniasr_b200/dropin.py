@@ -90,14 +90,92 @@ def _beam_step(self, s: int, ckeys: int, gkeys: int) -> None:
 
 EOS, PAD, LIMIT = 2, 1, 8188  # set from the reference's llm / decode modules by install()
 
+_WEIGHT_CLASS = None
 
-def install(package: str = "omniasr_trt") -> types.ModuleType:
-    """Swaps ``<package>.kernels`` for a module with this package's path functions; returns that module."""
+
+def _weight_class():
+    """A view class for the decoders' weights (``fuse_projections``' tuples, decode.py:34-54): ``x @ w.t()`` and
+    ``torch.addmm(h, x, w.t())`` with at most 64 bf16 token rows run :func:`kernels.decode_gemm` (store / residual);
+    every other use of the weight, and every other shape or dtype (the prefill's thousands of rows, an fp32 model),
+    is torch's own operation on the plain tensor."""
+    global _WEIGHT_CLASS
+    if _WEIGHT_CLASS is not None:
+        return _WEIGHT_CLASS
+    import torch
+
+    from . import kernels as ours
+
+    def plain(t):
+        return t.as_subclass(torch.Tensor) if isinstance(t, DecodeWeight) else t
+
+    def fits(x, w) -> bool:
+        return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+                and 1 <= x.size(0) <= 64 and x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0
+                and w.dim() == 2 and w.stride(1) == 1 and w.stride(0) % 8 == 0 and w.data_ptr() % 16 == 0
+                and x.size(1) == w.size(1) and x.size(1) % 8 == 0 and x.device == w.device)
+
+    class DecodeWeight(torch.Tensor):
+        _base = None  # on the view returned by .t(): the weight [n, k] itself
+
+        @classmethod
+        def __torch_function__(cls, func, types, args=(), kwargs=None):
+            kwargs = kwargs or {}
+            if func is torch.Tensor.t and len(args) == 1 and isinstance(args[0], DecodeWeight):
+                with torch._C.DisableTorchFunctionSubclass():
+                    w = plain(args[0])
+                    view = w.t().as_subclass(DecodeWeight)
+                view._base = w
+                return view
+            if func in (torch.matmul, torch.Tensor.matmul, torch.Tensor.__matmul__) and len(args) == 2 and not kwargs:
+                x, wt = args
+                if isinstance(wt, DecodeWeight) and wt._base is not None and not isinstance(x, DecodeWeight) \
+                        and fits(x, wt._base):
+                    return ours.decode_gemm(x, wt._base)
+            if func is torch.addmm and len(args) == 3 and not kwargs:
+                h, x, wt = args
+                if isinstance(wt, DecodeWeight) and wt._base is not None and not isinstance(x, DecodeWeight) \
+                        and not isinstance(h, DecodeWeight) and fits(x, wt._base) and h.dtype == torch.bfloat16 \
+                        and h.shape == (x.size(0), wt._base.size(0)) and h.stride(1) == 1 and h.stride(0) % 8 == 0 \
+                        and h.data_ptr() % 16 == 0:
+                    return ours.decode_gemm(x, wt._base, "residual", residual=h)
+            with torch._C.DisableTorchFunctionSubclass():
+                return func(*[plain(a) for a in args], **{k: plain(v) for k, v in kwargs.items()})
+
+    _WEIGHT_CLASS = DecodeWeight
+    return DecodeWeight
+
+
+def _routed_projections(fuse):
+    """``decode.fuse_projections`` whose tuples hold weight views that route the decode step's products."""
+
+    def fuse_projections(model):
+        cls = _weight_class()
+        return [tuple(w.as_subclass(cls) for w in layer) for layer in fuse(model)]
+
+    fuse_projections.reference = fuse
+    return fuse_projections
+
+
+def _route_products(package: str, gemm: bool) -> None:
+    decode = importlib.import_module(f"{package}.decode")
+    routed = getattr(decode.fuse_projections, "reference", None) is not None
+    if gemm and not routed:
+        decode.fuse_projections = _routed_projections(decode.fuse_projections)
+    elif not gemm and routed:
+        decode.fuse_projections = decode.fuse_projections.reference
+
+
+def install(package: str = "omniasr_trt", gemm: bool = False) -> types.ModuleType:
+    """Swaps ``<package>.kernels`` for a module with this package's path functions; returns that module. With
+    ``gemm``, decoders built afterwards also run their step's weight products with at most 64 bf16 token rows
+    (decode.py:201-205, spec.py:100-107, beam.py:148-154: the QKV, output, gate/inner and FFN-output projections) on
+    :func:`kernels.decode_gemm` instead of cuBLAS."""
     from . import kernels as ours
 
     pkg = importlib.import_module(package)
     ref = importlib.import_module(f"{package}.kernels")
     if getattr(ref, "__omniasr_b200__", False):
+        _route_products(package, gemm)
         return ref
     merged = types.ModuleType(f"{package}.kernels", ours.__doc__)
     for name in dir(ref):  # the reference's other names (propose, accept, ...) first
@@ -117,6 +195,7 @@ def install(package: str = "omniasr_trt") -> types.ModuleType:
     decode = importlib.import_module(f"{package}.decode")  # its prefill attention (decode.py:171)
     if not isinstance(decode.F, _Functional):
         decode.F = _Functional(ours.prefill_attention)
+    _route_products(package, gemm)
     beam = importlib.import_module(f"{package}.beam")  # its selection after the LM head (beam.py:161-187)
     llm = importlib.import_module(f"{package}.llm")
     global EOS, PAD, LIMIT

@@ -101,3 +101,20 @@ def test_repeated_calls_give_the_same_bits(rows, n, k, mode):
         again = K().decode_gemm(x, w, mode, residual=h)
         assert torch.equal(first.view(torch.int16), again.view(torch.int16))
     assert K().read_status() == 0
+
+
+def test_drop_in_weight_views_route_here():
+    """``dropin.install(gemm=True)``'s weight views: ``x @ w.t()`` and ``torch.addmm(h, x, w.t())`` with at most 64
+    bf16 rows are this GEMM (bit for bit the direct call); more rows are torch's own product."""
+    from omniasr_b200 import dropin
+
+    cls = dropin._weight_class()
+    x, w = data(40, 4096, 4096, 7)
+    h = torch.randn(40, 4096, device="cuda").to(torch.bfloat16)
+    v = w.as_subclass(cls)
+    assert torch.equal((x @ v.t()).view(torch.int16), K().decode_gemm(x, w).view(torch.int16))
+    assert torch.equal(torch.addmm(h, x, v.t()).view(torch.int16),
+                       K().decode_gemm(x, w, "residual", residual=h).view(torch.int16))
+    big = torch.randn(100, 4096, device="cuda").to(torch.bfloat16)
+    assert torch.equal(big @ v.t(), big @ w.t())
+    assert K().read_status() == 0
