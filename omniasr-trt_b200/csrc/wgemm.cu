@@ -180,7 +180,7 @@ OMNI_DEV void finish_rows(const GemmArgs& a, int tile, int row, const float* xch
 // of the 128 participating threads, which all call this together (named barrier `bar`).
 template <int NT, int MODE>
 OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&acc)[NT], float* xch, int bar) {
-  if (MODE == kGemmRope) {
+  if constexpr (MODE == kGemmRope) {
     // The tile's 128 features are dims d0..d0+127 of one head h of section q / k / v (128 divides the head_dim);
     // thread `row` holds dim d0 + row, so a rotation pair (2j, 2j + 1) is two neighbouring lanes (one shuffle).
     // Each product is rounded to bf16 first, as the GEMM's output would be, then rotated in fp32 with the
@@ -252,14 +252,14 @@ OMNI_DEV void finish_tile(const GemmArgs& a, int tile, int row, const float (&ac
       }
     }
     named_sync(bar, 128);  // the stage is free again
-    return;
-  }
-  // Store / residual / SwiGLU: the tile goes through shared memory (`xch`, [NT][128] fp32, thread `row` writes
-  // column `row`), then finish_rows writes it out.
+  } else {
+    // Store / residual / SwiGLU: the tile goes through shared memory (`xch`, [NT][128] fp32, thread `row` writes
+    // column `row`), then finish_rows writes it out.
 #pragma unroll
-  for (int m = 0; m < NT; ++m) xch[m * BM + row] = acc[m];
-  named_sync(bar, 128);
-  finish_rows<NT, MODE>(a, tile, row, xch, 0, a.rows, bar);
+    for (int m = 0; m < NT; ++m) xch[m * BM + row] = acc[m];
+    named_sync(bar, 128);
+    finish_rows<NT, MODE>(a, tile, row, xch, 0, a.rows, bar);
+  }
 }
 
 template <int NT, int MODE>
