@@ -67,7 +67,11 @@ constexpr int W_BYTES = KB * W_BOX;
 #define OMNI_WGEMM_STAGES (8 / OMNI_WGEMM_KB)
 #endif
 constexpr int STAGES = OMNI_WGEMM_STAGES;
-constexpr int kMaxCluster = 4;  // CTAs per tile in cluster mode (the reduction is unrolled over this many ranks)
+constexpr int kMaxCluster = 4;
+#ifndef OMNI_WGEMM_LATE_WATCH_NS
+#define OMNI_WGEMM_LATE_WATCH_NS 3000
+#endif
+constexpr uint64_t kLateWatchNs = OMNI_WGEMM_LATE_WATCH_NS;  // the watch past the own accumulator (ns)  // CTAs per tile in cluster mode (the reduction is unrolled over this many ranks)
 constexpr int THREADS = 192;
 
 template <int NT>
@@ -459,13 +463,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       float others[NT];
       bool early = false;
       if (!whole && me == b0) {
+        // The watch goes on for a short while after the own accumulator is ready: a contributor that covers the
+        // middle of the tile finishes at about the same time, and one more wait for its arrival is shorter than
+        // the chain of the arrive-and-sum path.
         const uint64_t t0 = global_ns();
+        uint64_t t_acc = 0;
         int f = 0;
         do {
           if (row == 0) {
             // a relaxed poll; the fence below orders the partial loads after the arrivals it saw
             int v = ld_relaxed_gpu(&a.counters[t]) == b1 - b0 ? 1 : 0;
-            if (!v && mbar_test_wait(&acc_full[buf], (seg >> 1) & 1)) v = 2;
+            if (!v && (t_acc != 0 || mbar_test_wait(&acc_full[buf], (seg >> 1) & 1))) {
+              const uint64_t now = global_ns();
+              if (t_acc == 0) t_acc = now;
+              if (now - t_acc > kLateWatchNs) v = 2;
+            }
             if (!v && global_ns() - t0 > kWaitLimitNs) v = 3;
             *last_flag = v;
           }
