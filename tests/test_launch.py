@@ -20,10 +20,10 @@ from omniasr_b200.launch import WorkerFailed, run_sharded
 
 
 def _reference_src() -> str:
-    """The reference package: baseline/_ref (placed by the build), else the checkout's src/ in the build container."""
-    for p in (ROOT / "baseline" / "_ref", "/root/reference/src"):
-        if os.path.exists(os.path.join(str(p), "omniasr_trt", "decode.py")):
-            return str(p)
+    """The reference package, as __graft_entry__.build() places it in baseline/_ref."""
+    p = ROOT / "baseline" / "_ref"
+    if os.path.exists(os.path.join(str(p), "omniasr_trt", "decode.py")):
+        return str(p)
     pytest.fail("the reference package is missing (run __graft_entry__.build())")
 
 
