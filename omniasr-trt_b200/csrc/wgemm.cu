@@ -18,6 +18,15 @@
 // needed. Roles (192 threads): warp 0 TMA (weight boxes + token boxes per stage), warp 1 MMA issuer, warps 2-5
 // epilogue (thread = weight row = TMEM lane).
 //
+// Cluster mode, for few long tiles (the 4096-wide projections: 32 tiles on 148 SMs, where stream-K would cut each
+// tile between four or five CTAs that all finish at the end): a cluster of up to 4 CTAs per tile, each streaming a
+// contiguous share of its chunks; after the role loops the partials are summed through distributed shared memory in
+// rank order and each CTA writes out a share of the token rows.
+//
+// Launch: programmatic dependent. The first stages' weight boxes are requested before the dependency wait (the
+// weights must not come from the kernel before), and the producer lets the next kernel launch once it has issued
+// its last load.
+//
 // SwiGLU: the gate and inner rows of the same 64 outputs are two 64-row boxes of one 128-row tile (no weight copy),
 // so the epilogue forms inner * silu(gate) within the tile.
 
