@@ -412,7 +412,9 @@ def decode_gemm(x: torch.Tensor, w: torch.Tensor, mode: str = "store", residual:
     """The decoder step's weight GEMMs for at most 64 token rows (bf16): ``x @ w.t()`` ("store"),
     ``torch.addmm(residual, x, w.t())`` ("residual"), or with ``w`` the concatenated [gate; inner] weights
     ``inner * F.silu(gate)`` of ``(x @ w.t()).chunk(2, -1)`` ("swiglu", each half rounded to bf16 first, as the
-    reference computes it). Rows of x and w must be contiguous with 16-byte aligned strides."""
+    reference computes it). Rows of x and w must be contiguous with 16-byte aligned strides. The kernel requests its
+    first weight tiles before waiting for the kernel launched before it on the stream, so ``w`` must not be written
+    by that kernel (decoder weights are not); x and the residual may be."""
     rows, k = x.shape
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
         raise ValueError("decode_gemm: bf16 x and w")
@@ -440,7 +442,8 @@ def decode_gemm_rope(x: torch.Tensor, w: torch.Tensor, cs: torch.Tensor, pos: to
                      cache_pos: torch.Tensor | None = None) -> torch.Tensor:
     """``rope_kv(x @ w.t(), cs, pos, k_cache, v_cache, heads, slots, cache_pos)`` in one kernel (bf16, at most 64
     token rows, head_dim a multiple of 128): the QKV product's epilogue rotates q and k and appends k and v to the
-    caches; returns q [N, heads, D]. The product is rounded to bf16 before the rotation, as the GEMM's output is."""
+    caches; returns q [N, heads, D]. The product is rounded to bf16 before the rotation, as the GEMM's output is.
+    As for :func:`decode_gemm`, ``w`` must not be written by the kernel launched just before on the stream."""
     rows, k = x.shape
     n = w.size(0)
     dim = n // (3 * heads)
