@@ -76,11 +76,11 @@ constexpr int W_BYTES = KB * W_BOX;
 #define OMNI_WGEMM_STAGES (8 / OMNI_WGEMM_KB)
 #endif
 constexpr int STAGES = OMNI_WGEMM_STAGES;
-constexpr int kMaxCluster = 4;
+constexpr int kMaxCluster = 4;  // CTAs per tile in cluster mode (the reduction is unrolled over this many ranks)
 #ifndef OMNI_WGEMM_LATE_WATCH_NS
 #define OMNI_WGEMM_LATE_WATCH_NS 3000
 #endif
-constexpr uint64_t kLateWatchNs = OMNI_WGEMM_LATE_WATCH_NS;  // the watch past the own accumulator (ns)  // CTAs per tile in cluster mode (the reduction is unrolled over this many ranks)
+constexpr uint64_t kLateWatchNs = OMNI_WGEMM_LATE_WATCH_NS;  // the watch past the own accumulator (ns)
 constexpr int THREADS = 192;
 
 template <int NT>
