@@ -161,7 +161,8 @@ OMNI_DEV void finish_rows(const GemmArgs& a, int tile, int row, const float* xch
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float gq = bf16r(g[q]);
-        const float sq = bf16r(gq / (1.f + __expf(-gq)));
+        // silu(g) = g / (1 + e^-g); the fast divide's few-ulp error is far below the bf16 rounding that follows
+        const float sq = bf16r(__fdividef(gq, 1.f + __expf(-gq)));
         v[q] = bf16r(u[q]) * sq;
       }
     } else {
